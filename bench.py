@@ -1,0 +1,397 @@
+#!/usr/bin/env python3
+"""Benchmark: bf16 weight rows -> GGML blocks on B200, the reference's headline metric.
+
+Workload (the metric's quoted config that fits one GPU):
+Q4_K with imatrix (--pure) over eight bf16 tensors, 4 x (4096 x 4096) and 4 x (14336 x 4096),
+N(0, 0.02) with 0.1 % N(0, 0.5) outliers, per-column imatrix lognormal(0, 1.5). Synthetic
+data generated on the device from fixed seeds; 302 M values = 604 MB of bf16 per step, larger
+than the 126 MB L2, so no L2 flush is needed between steps.
+
+One step = quantize all eight tensors (eight kernel launches). N GPUs: one process per GPU,
+each quantizes its own tensor set (weak scaling, no collective on the data path; NCCL is used
+only for the barrier and the max-over-ranks of the timings).
+
+  value  input GB/s with inputs resident in HBM (whole job, all ranks)
+  e2e    the same metric through the public API from pinned host buffers: per step every
+         tensor is copied host->device, quantized and its blocks copied back to host, with
+         copies and kernels overlapped on two streams
+  roofline  the Q4_K kernel against the FP32 lane-op ceiling (148 SMs x 128 lanes x SM clock):
+         algorithmic ops = 655 per value (37 x 17 per candidate step + 11 initial + 3 sums
+         + 5 weights + 7 requant/pack); plus the HBM view of the same launches
+--impl reference: the CPU restatement of the reference's algorithm (oracle/) on all host
+cores over a bounded sample of the same workload (the reference itself is Python/torch and
+cannot travel to the GPU host; oracle/ is its bit-exact C port).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "quant-studio_b200"))
+sys.path.insert(0, str(ROOT))
+
+SHAPES_C2 = [(4096, 4096)] * 4 + [(14336, 4096)] * 4
+NAMES_C2 = [f"blk.{i}.attn_q.weight" for i in range(4)] + [f"blk.{i}.ffn_up.weight" for i in range(4)]
+# algorithmic FP32 lane ops per value for each (type, imatrix) the bench can time
+ALG_OPS = {("q4_k", True): 655, ("q4_k", False): 21 * 17 + 11 + 3 + 4 + 7,
+           ("q6_k", False): 19 * 9 + 20, ("q6_k", True): 19 * 9 + 18, ("q4_0", False): 10}
+ALG_BYTES_OUT = {"q4_0": 18 / 32, "q2_k": 84 / 256, "q3_k": 110 / 256, "q4_k": 144 / 256,
+                 "q5_k": 176 / 256, "q6_k": 210 / 256, "iq4_xs": 136 / 256, "iq2_xxs": 66 / 256,
+                 "iq2_xs": 74 / 256, "iq2_s": 82 / 256, "iq3_xxs": 98 / 256, "iq3_s": 110 / 256}
+TYPE_IDS = {"q4_0": 2, "q2_k": 10, "q3_k": 11, "q4_k": 12, "q5_k": 13, "q6_k": 14, "iq2_xxs": 16,
+            "iq2_xs": 17, "iq3_xxs": 18, "iq3_s": 21, "iq2_s": 22, "iq4_xs": 23}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        if not self.rows:
+            return None
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def make_inputs(torch, device, seed: int, shapes):
+    """Seeded synthetic bf16 weights + lognormal imatrix, generated on the device."""
+    g = torch.Generator(device=device)
+    xs, qws = [], []
+    for i, (r, c) in enumerate(shapes):
+        g.manual_seed(seed * 1000 + i)
+        x = torch.empty((r, c), dtype=torch.float32, device=device).normal_(0.0, 0.02, generator=g)
+        out = torch.rand((r, c), device=device, generator=g) < 0.001
+        x[out] = torch.empty(int(out.sum()), device=device).normal_(0.0, 0.5, generator=g)
+        xs.append(x.to(torch.bfloat16))
+        del x, out
+        qws.append(torch.empty(c, device=device).log_normal_(0.0, 1.5, generator=g))
+    return xs, qws
+
+
+def run_reference(args, config: dict) -> None:
+    """The reference arm: the CPU port of the reference algorithm on all host threads."""
+    import oracle
+
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(1)
+    k = 4096
+    qw = rng.lognormal(0.0, 1.5, k).astype(np.float32)
+
+    def sample(rows):
+        a = rng.normal(0.0, 0.02, (rows, k))
+        m = rng.random(a.shape) < 0.001
+        a[m] = rng.normal(0.0, 0.5, int(m.sum()))
+        # bf16-representable values, as the bf16 weights are
+        return ((a.astype(np.float32).view(np.uint32) + 0x8000) & 0xFFFF0000).view(np.float32)
+
+    oracle.quantize(args.qtype, sample(8), qw, nthreads=1)  # one-time table set-up
+    probe = sample(256)
+    t0 = time.perf_counter()
+    oracle.quantize(args.qtype, probe, qw if args.imatrix else None, nthreads=cores)
+    rate = probe.size / max(time.perf_counter() - t0, 1e-6)
+    rows = int(min(8192, max(64, rate * args.ref_seconds / k)))
+    x = sample(rows)
+    for _ in range(args.warmup):
+        oracle.quantize(args.qtype, x[:64], qw if args.imatrix else None, nthreads=cores)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.quantize(args.qtype, x, qw if args.imatrix else None, nthreads=cores)
+        times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
+    gbs = x.size * 2 / dt / 1e9
+    line = {"impl": "reference", "metric": "input GB/s quantized (bf16->q4_k, imatrix)", "value": round(gbs, 6),
+            "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": round(gbs, 6), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{rows} rows x {k} bf16 values per step ({x.size * 2 / 1e6:.1f} MB) "
+                                       f"of the benchmark distribution, median of {args.steps} steps"},
+            "e2e": {"value": round(gbs, 6), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="qsb200", choices=["qsb200", "reference"])
+    ap.add_argument("--qtype", default="q4_k")
+    ap.add_argument("--no-imatrix", dest="imatrix", action="store_false")
+    ap.add_argument("--ref-seconds", type=float, default=1.0, help="CPU seconds per reference step")
+    ap.add_argument("--no-e2e", dest="e2e", action="store_false")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n_elem = sum(r * c for r, c in SHAPES_C2)
+    config = {"workload": f"BASELINE configs[1]: {args.qtype}{' + imatrix' if args.imatrix else ''} --pure over "
+                          f"4 x 4096x4096 + 4 x 14336x4096 bf16 tensors per GPU",
+              "tensors": len(SHAPES_C2), "values_per_gpu": n_elem, "input_bytes_per_gpu": 2 * n_elem,
+              "l2": "inputs 604 MB/GPU > 126 MB L2: no flush needed", "parallelism": f"shard{world}"}
+
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, config)
+        return
+
+    import torch
+
+    from kernels import _native
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    gt = TYPE_IDS[args.qtype]
+    xs, qws = make_inputs(torch, device, seed=rank, shapes=SHAPES_C2)
+    if not args.imatrix:
+        qws = [None] * len(xs)
+    outs = [torch.empty((x.shape[0], _native.row_bytes(gt, x.shape[1])), dtype=torch.uint8, device=device)
+            for x in xs]
+    stream = torch.cuda.Stream(device)
+
+    def step(evs=None):
+        for i, (x, q, o) in enumerate(zip(xs, qws, outs)):
+            if evs is not None:
+                evs[i][0].record(stream)
+            _native.quantize_into(gt, x, q, o, stream)
+            if evs is not None:
+                evs[i][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    kev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in xs]
+           for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        t_start.record(stream)
+        for s in range(args.steps):
+            step(kev[s])
+        t_end.record(stream)
+        stream.synchronize()
+        barrier()
+    ms_total = t_start.elapsed_time(t_end)
+    kern_ms = [[a.elapsed_time(b) for a, b in ev] for ev in kev]
+    launch_ms = sum(sum(k) for k in kern_ms) / (args.steps * len(xs))
+
+    def allmax(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms_total = allmax(ms_total)
+    ms_step = ms_total / args.steps
+    value = world * 2 * n_elem / (ms_step * 1e-3) / 1e9
+
+    # roofline of the quantize kernel: lane ops (compute bound) and bytes (HBM view)
+    clocks = clk.summary()
+    peaks = measured_peaks()
+    sm_count = torch.cuda.get_device_properties(device).multi_processor_count
+    sm_mhz = (clocks or {}).get("sm_mhz") or peaks.get("clocks_under_load", {}).get("sm_mhz_median") or 1965.0
+    ops = ALG_OPS.get((args.qtype, args.imatrix))
+    elems_per_launch = n_elem / len(xs)
+    alg_bytes = elems_per_launch * (2 + ALG_BYTES_OUT[args.qtype])
+    hbm = {"bound": "hbm", "achieved": round(alg_bytes / (launch_ms * 1e-3) / 1e9, 2), "peak": peaks["hbm_gbs"],
+           "unit": "GB/s", "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"}
+    hbm["frac"] = round(hbm["achieved"] / hbm["peak"], 4)
+    if ops is not None:
+        lane_peak = sm_count * 128 * sm_mhz * 1e6 / 1e12
+        roof = {"bound": "fp32-lane", "achieved": round(ops * elems_per_launch / (launch_ms * 1e-3) / 1e12, 3),
+                "peak": round(lane_peak, 3), "unit": "Tops/s",
+                "peak_source": f"{sm_count} SMs x 128 FP32 lanes x {sm_mhz:.0f} MHz median SM clock in the timed region",
+                "ops_per_value": ops, "hbm": hbm, "traffic": None}
+        roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
+    else:
+        roof = dict(hbm, traffic=None)
+    prof = ROOT / "profiles" / f"traffic_{args.qtype}{'_imat' if args.imatrix else ''}.json"
+    if prof.exists():
+        roof["traffic"] = json.loads(prof.read_text()).get("bytes_per_value_launch")
+        if roof["traffic"] is not None:
+            roof["traffic"] = round(roof["traffic"] * elems_per_launch)
+
+    # end to end through the public API from pinned host memory
+    e2e = None
+    if args.e2e:
+        e2e = e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, world, n_elem)
+
+    line = {"metric": f"input GB/s quantized (bf16->{args.qtype}{', imatrix' if args.imatrix else ''})",
+            "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded, generated on device; random-init weights of the config shapes)",
+            "config": config, "roofline": roof, "clocks": clocks, "gpu_launches": args.steps * len(xs),
+            "kernel_ms_per_launch": round(launch_ms, 4), "e2e": e2e}
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, world, n_elem):
+    """Host-buffer pipeline: chunks of rows go H2D on one stream, are quantized and copied
+    back on another; events order the two so copies overlap the kernels."""
+    chunk_rows = 2048
+    h_in = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs]
+    for h, x in zip(h_in, xs):
+        h.copy_(x)
+    h_out = [torch.empty(o.shape, dtype=torch.uint8, pin_memory=True) for o in outs]
+    s_h2d, s_comp, s_d2h = (torch.cuda.Stream(device) for _ in range(3))
+    nbuf = 3
+    kmax = max(x.shape[1] for x in xs)
+    d_in = [torch.empty((chunk_rows, kmax), dtype=torch.bfloat16, device=device) for _ in range(nbuf)]
+    d_out = [torch.empty((chunk_rows, max(o.shape[1] for o in outs)), dtype=torch.uint8, device=device)
+             for _ in range(nbuf)]
+    h2d_done, kern_done, d2h_done = ([torch.cuda.Event() for _ in range(nbuf)] for _ in range(3))
+    launches = [0]
+
+    def one_step():
+        slot = 0
+        for x_h, q, o_h in zip(h_in, qws, h_out):
+            n, k = x_h.shape
+            rb = o_h.shape[1]
+            for r0 in range(0, n, chunk_rows):
+                r = min(chunk_rows, n - r0)
+                din = d_in[slot][:r, :k]
+                dout = d_out[slot][:r, :rb]
+                s_h2d.wait_event(kern_done[slot])       # the slot's previous kernel has read d_in
+                with torch.cuda.stream(s_h2d):
+                    din.copy_(x_h[r0:r0 + r], non_blocking=True)
+                h2d_done[slot].record(s_h2d)
+                s_comp.wait_event(h2d_done[slot])
+                s_comp.wait_event(d2h_done[slot])       # the slot's previous blocks are on the host
+                _native.quantize_into(gt, din, q, dout, s_comp)
+                launches[0] += 1
+                kern_done[slot].record(s_comp)
+                s_d2h.wait_event(kern_done[slot])
+                with torch.cuda.stream(s_d2h):
+                    o_h[r0:r0 + r].copy_(dout, non_blocking=True)
+                d2h_done[slot].record(s_d2h)
+                slot = (slot + 1) % nbuf
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    launches[0] = 0
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s_h2d)
+    for _ in range(args.steps):
+        one_step()
+    s_h2d.wait_stream(s_comp)
+    s_h2d.wait_stream(s_d2h)
+    t1.record(s_h2d)
+    torch.cuda.synchronize()
+    ms = allmax(t0.elapsed_time(t1)) / args.steps
+    ok = all(torch.equal(o_h.to(device), o) for o_h, o in zip(h_out, outs))
+    return {"value": round(world * 2 * n_elem / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+            "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in xs)),
+            "d2h_bytes_per_step": int(sum(o.numel() for o in outs)), "ms_per_step": round(ms, 3),
+            "gpu_launches": launches[0], "pipeline": f"{chunk_rows}-row chunks, {nbuf} device slots, H2D / kernel / D2H streams",
+            "matches_device_resident_output": ok}
+
+
+def cpu_baseline(args) -> dict:
+    """The oracle (C port of the reference algorithm) on this host's cores, bounded sample."""
+    import oracle
+
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(2)
+    k = 4096
+    qw = rng.lognormal(0.0, 1.5, k).astype(np.float32) if args.imatrix else None
+    oracle.quantize(args.qtype, rng.normal(0.0, 0.02, (8, k)).astype(np.float32), qw, nthreads=1)
+    a = rng.normal(0.0, 0.02, (256, k)).astype(np.float32)
+    t0 = time.perf_counter()
+    oracle.quantize(args.qtype, a, qw, nthreads=cores)
+    rate = a.size / max(time.perf_counter() - t0, 1e-6)
+    rows = int(min(16384, max(64, rate * 10.0 / k)))
+    a = rng.normal(0.0, 0.02, (rows, k))
+    m = rng.random(a.shape) < 0.001
+    a[m] = rng.normal(0.0, 0.5, int(m.sum()))
+    a = ((a.astype(np.float32).view(np.uint32) + 0x8000) & 0xFFFF0000).view(np.float32)
+    t0 = time.perf_counter()
+    oracle.quantize(args.qtype, a, qw, nthreads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": round(a.size * 2 / dt / 1e9, 6), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{rows} rows x {k} values ({a.size * 2 / 1e6:.1f} MB bf16) of the benchmark distribution, "
+                      f"{dt:.1f} s on {cores} threads"}
+
+
+if __name__ == "__main__":
+    main()

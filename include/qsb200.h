@@ -1,0 +1,99 @@
+/*
+ * qsb200: B200 (sm_100a) GGUF block quantizers behind a plain C ABI.
+ *
+ * Drop-in boundary for the per-type kernels of ngxson/quant-studio. In the reference a
+ * kernel is obtained as `QuantSpec.make_kernel(device, qw)` (kernels/common.py:27-37)
+ * and called as `quant_fn(x)` on an (n_rows, k) float32 device tensor, returning a
+ * new (n_rows, k // QK * block_bytes) uint8 tensor (quant-studio.py:456, :198). The
+ * entry points below replace that call: the caller owns every buffer, passes the
+ * source rows in bf16 / f16 / f32 directly (the reference's f32 upcast at
+ * quant-studio.py:197 is not needed) and a CUDA stream; work is enqueued on that
+ * stream and the call returns without synchronizing.
+ *
+ * Type ids are gguf GGMLQuantizationType values; source types are GGML F32 (0),
+ * F16 (1) and BF16 (30). Every function returns QS_OK (0) or a negative QS_E* code;
+ * qs_last_error() gives the message of the calling thread's last failure.
+ */
+#ifndef QSB200_H
+#define QSB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QSB200_VERSION 1
+
+#define QS_OK 0
+#define QS_EINVAL (-1)    /* bad argument: type, k, alignment, null pointer, stride */
+#define QS_ECUDA (-2)     /* a CUDA call failed; see qs_last_error() */
+#define QS_ENOTSUP (-3)   /* type id not implemented */
+#define QS_ENOIMAT (-4)   /* the type needs importance weights and qw was NULL */
+
+/* GGML type ids this library quantizes to (gguf GGMLQuantizationType). */
+#define QS_TYPE_Q4_0 2
+#define QS_TYPE_Q2_K 10
+#define QS_TYPE_Q3_K 11
+#define QS_TYPE_Q4_K 12
+#define QS_TYPE_Q5_K 13
+#define QS_TYPE_Q6_K 14
+#define QS_TYPE_IQ2_XXS 16
+#define QS_TYPE_IQ2_XS 17
+#define QS_TYPE_IQ3_XXS 18
+#define QS_TYPE_IQ3_S 21
+#define QS_TYPE_IQ2_S 22
+#define QS_TYPE_IQ4_XS 23
+
+/* Source element types (GGML ids); the reference's TORCH_DTYPES (kernels/common.py:20-24). */
+#define QS_SRC_F32 0
+#define QS_SRC_F16 1
+#define QS_SRC_BF16 30
+
+/* Library version (QSB200_VERSION). */
+int qs_version(void);
+
+/* Prepare `device` (SM count, lattice tables). Idempotent and thread-safe; qs_quantize
+ * calls it lazily for the current device. Replaces the per-device table caches of the
+ * reference (kernels/iq2.py:77-84 tables_for, iq2xs_common.py:98-106, iq3_common.py:78-85). */
+int qs_init(int device);
+
+/* 1 if `ggml_type` is implemented, else 0 (the reference's QUANT_TYPES registry,
+ * kernels/__init__.py:18-27). */
+int qs_type_supported(int ggml_type);
+
+/* 1 if the kernel cannot run without importance weights (IQ2_XXS, IQ2_XS, IQ2_S:
+ * kernels/iq2.py:418, iq2_xs.py:20, iq2_s.py:21 take qw unconditionally). */
+int qs_type_needs_qw(int ggml_type);
+
+/* Block geometry: values per block (*qk) and packed bytes per block (*block_bytes);
+ * the gguf GGML_QUANT_SIZES entry the reference uses (quant-studio.py:143-145). */
+int qs_block_info(int ggml_type, int* qk, int* block_bytes);
+
+/* Packed bytes of one row of k values: k / qk * block_bytes (quant-studio.py:143-145). */
+int qs_row_bytes(int ggml_type, int64_t k, int64_t* out_bytes);
+
+/*
+ * Quantize n_rows x k source values into packed GGML blocks.
+ * Replaces quant_fn(x) (the `quantize_<type>(x, qw)` functions, e.g.
+ * kernels/q4_k.py:25-79, kernels/iq2.py:418-498) as called at quant-studio.py:198.
+ *   src            device pointer, n_rows x k elements of src_type, rows contiguous,
+ *                  16-byte aligned
+ *   qw             device pointer to k float32 importance weights (16-byte aligned),
+ *                  or NULL for the no-imatrix variant
+ *   dst            device pointer; row r is written at dst + r * dst_row_bytes
+ *   dst_row_bytes  >= qs_row_bytes(type, k)
+ *   stream         cudaStream_t (NULL = legacy default stream)
+ * Output bytes are identical to the reference's eager CPU path for the same values.
+ */
+int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_rows, int64_t k,
+                const float* qw, void* dst, int64_t dst_row_bytes, void* stream);
+
+/* Message of the calling thread's last failure ("" if none). */
+const char* qs_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QSB200_H */

@@ -687,6 +687,10 @@ static void grid_build(grid_t *g, const uint16_t *codes, int grid_size, int bits
             g->len[c] = 1;
             continue;
         }
+        /* 2-bit sweeps clamp levels to 0..2, so codes with a level 3 are never looked up */
+        int reachable = 1;
+        for (int j = 0; j < npos && bits == 2; j++) reachable &= ((c >> (2 * j)) & 3) != 3;
+        if (!reachable) continue;
         for (int i = 0; i < grid_size; i++) {
             int d2 = 0;
             for (int j = 0; j < npos; j++) {

@@ -1,0 +1,165 @@
+// C ABI of libqsb200 (declared in include/qsb200.h): argument checks, per-device
+// state, dispatch to the kernel files.
+#include <mutex>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "../../include/qsb200.h"
+#include "qs_kernels.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(QS_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+struct TypeInfo {
+    int type, qk, bytes, needs_qw;
+};
+
+const TypeInfo kTypes[] = {
+    {qs::QS_Q4_0, 32, 18, 0},      {qs::QS_Q2_K, 256, 84, 0},      {qs::QS_Q3_K, 256, 110, 0},
+    {qs::QS_Q4_K, 256, 144, 0},    {qs::QS_Q5_K, 256, 176, 0},     {qs::QS_Q6_K, 256, 210, 0},
+    {qs::QS_IQ2_XXS, 256, 66, 1},  {qs::QS_IQ2_XS, 256, 74, 1},    {qs::QS_IQ3_XXS, 256, 98, 0},
+    {qs::QS_IQ3_S, 256, 110, 0},   {qs::QS_IQ2_S, 256, 82, 1},     {qs::QS_IQ4_XS, 256, 136, 0},
+};
+
+const TypeInfo* find_type(int t) {
+    for (const auto& ti : kTypes)
+        if (ti.type == t) return &ti;
+    return nullptr;
+}
+
+bool is_iq(int t) {
+    return t == qs::QS_IQ2_XXS || t == qs::QS_IQ2_XS || t == qs::QS_IQ2_S || t == qs::QS_IQ3_XXS || t == qs::QS_IQ3_S;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+    bool ready = false;
+    int num_sms = 0;
+    qs::IqTables* iq = nullptr;
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+
+// Caller holds no lock; the device must be current.
+int ensure_device(int device, DeviceState** out) {
+    if (device < 0 || device >= kMaxDevices) return fail(QS_EINVAL, "device %d out of range", device);
+    std::lock_guard<std::mutex> lk(g_mu);
+    DeviceState& d = g_dev[device];
+    if (!d.ready) {
+        cudaError_t e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+        e = qs::iq_tables_create(&d.iq);
+        if (e != cudaSuccess) return cuda_fail(e, "uploading lattice tables");
+        d.ready = true;
+    }
+    *out = &d;
+    return QS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+#define QS_API __attribute__((visibility("default")))
+
+QS_API int qs_version(void) { return QSB200_VERSION; }
+
+QS_API const char* qs_last_error(void) { return g_err; }
+
+QS_API int qs_type_supported(int ggml_type) { return find_type(ggml_type) != nullptr; }
+
+QS_API int qs_type_needs_qw(int ggml_type) {
+    const TypeInfo* ti = find_type(ggml_type);
+    return ti ? ti->needs_qw : 0;
+}
+
+QS_API int qs_block_info(int ggml_type, int* qk, int* block_bytes) {
+    const TypeInfo* ti = find_type(ggml_type);
+    if (!ti) return fail(QS_ENOTSUP, "ggml type %d is not supported", ggml_type);
+    if (qk) *qk = ti->qk;
+    if (block_bytes) *block_bytes = ti->bytes;
+    return QS_OK;
+}
+
+QS_API int qs_row_bytes(int ggml_type, int64_t k, int64_t* out_bytes) {
+    const TypeInfo* ti = find_type(ggml_type);
+    if (!ti) return fail(QS_ENOTSUP, "ggml type %d is not supported", ggml_type);
+    if (k <= 0 || k % ti->qk) return fail(QS_EINVAL, "row length %lld is not a positive multiple of %d", (long long)k, ti->qk);
+    if (out_bytes) *out_bytes = k / ti->qk * ti->bytes;
+    return QS_OK;
+}
+
+QS_API int qs_init(int device) {
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    DeviceState* d = nullptr;
+    int rc = ensure_device(device, &d);
+    if (prev != device) cudaSetDevice(prev);
+    return rc;
+}
+
+QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_rows, int64_t k, const float* qw,
+                void* dst, int64_t dst_row_bytes, void* stream) {
+    const TypeInfo* ti = find_type(ggml_type);
+    if (!ti) return fail(QS_ENOTSUP, "ggml type %d is not supported", ggml_type);
+    if (src_type != QS_SRC_F32 && src_type != QS_SRC_F16 && src_type != QS_SRC_BF16)
+        return fail(QS_EINVAL, "source type %d is not F32/F16/BF16", src_type);
+    if (k <= 0 || k % ti->qk) return fail(QS_EINVAL, "row length %lld is not a positive multiple of %d", (long long)k, ti->qk);
+    if (n_rows < 0) return fail(QS_EINVAL, "negative row count");
+    const int64_t row_bytes = k / ti->qk * ti->bytes;
+    if (dst_row_bytes < row_bytes) return fail(QS_EINVAL, "dst_row_bytes %lld < packed row size %lld", (long long)dst_row_bytes, (long long)row_bytes);
+    if (ti->needs_qw && !qw) return fail(QS_ENOIMAT, "ggml type %d needs importance weights (qw)", ggml_type);
+    if (n_rows == 0) return QS_OK;
+    if (!src || !dst) return fail(QS_EINVAL, "null src or dst");
+    if (((uintptr_t)src & 15) || (qw && ((uintptr_t)qw & 15)))
+        return fail(QS_EINVAL, "src and qw must be 16-byte aligned");
+
+    // run on the device that owns src (the runtime's current device may belong to another
+    // runtime instance in the process, e.g. the one torch links)
+    cudaPointerAttributes pa;
+    cudaError_t e = cudaPointerGetAttributes(&pa, src);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes(src)");
+    if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+        return fail(QS_EINVAL, "src is not device memory");
+    const int device = pa.device;
+    int cur = -1;
+    if ((e = cudaGetDevice(&cur)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != device && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    DeviceState* d = nullptr;
+    int rc = ensure_device(device, &d);
+    if (rc) return rc;
+
+    qs::QuantArgs a;
+    a.src = src;
+    a.src_type = src_type;
+    a.n_rows = n_rows;
+    a.k = k;
+    a.qw = qw;
+    a.dst = static_cast<uint8_t*>(dst);
+    a.dst_row_bytes = dst_row_bytes;
+    a.row_bytes = row_bytes;
+    a.nblk_row = k / ti->qk;
+    a.nblk = n_rows * a.nblk_row;
+    qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
+    e = is_iq(ggml_type) ? qs::launch_iq(ggml_type, a, ctx, d->iq) : qs::launch_kquant(ggml_type, a, ctx);
+    if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
+    return QS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,231 @@
+// Shared device helpers for the qs-b200 block quantizers (sm_100a).
+//
+// Every kernel here reproduces the reference's eager torch arithmetic bit for bit, so:
+//   - the library is built with -fmad=false: no mul+add contraction anywhere;
+//   - divides and square roots are IEEE round-to-nearest (-prec-div / -prec-sqrt);
+//   - torch.round is rintf (half to even);
+//   - sums keep the association of the reference site they restate: seq (left to
+//     right from the first term), tree (adjacent pairs), or torch's CPU cascade for
+//     `.sum(-1)` (8 lane partials, then a left-to-right pass seeded with +0).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace qs {
+
+constexpr int QK_K = 256;
+constexpr float EPS15 = 1e-15f;
+constexpr float EPS8 = 1e-8f;
+constexpr float F32_TINY = 1.17549435e-38f;
+
+// Source element types (GGML type ids).
+enum SrcType : int { SRC_F32 = 0, SRC_F16 = 1, SRC_BF16 = 30 };
+
+// ---------------------------------------------------------------------------
+// loads: n consecutive source elements -> f32 registers (exact conversions)
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ void load_row(const void* base, int64_t elem0, int src, float* v) {
+    if (src == SRC_F32) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + elem0);
+#pragma unroll
+        for (int i = 0; i < N / 4; i++) {
+            float4 t = __ldg(p + i);
+            v[4 * i + 0] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+        }
+    } else {
+        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + elem0);
+#pragma unroll
+        for (int i = 0; i < N / 8; i++) {
+            uint4 t = __ldg(p + i);
+            uint32_t w4[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                uint32_t lo = w4[j] & 0xFFFFu, hi = w4[j] >> 16;
+                if (src == SRC_BF16) {
+                    v[8 * i + 2 * j] = __uint_as_float(lo << 16);
+                    v[8 * i + 2 * j + 1] = __uint_as_float(hi << 16);
+                } else {
+                    v[8 * i + 2 * j] = __half2float(__ushort_as_half((unsigned short)lo));
+                    v[8 * i + 2 * j + 1] = __half2float(__ushort_as_half((unsigned short)hi));
+                }
+            }
+        }
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void load_f32(const float* p, float* v) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int i = 0; i < N / 4; i++) {
+        float4 t = __ldg(q + i);
+        v[4 * i + 0] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// exact scalar helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float rcp_rn(float x) { return __fdiv_rn(1.0f, x); }
+__device__ __forceinline__ float clampf(float x, float lo, float hi) { return x < lo ? lo : (x > hi ? hi : x); }
+__device__ __forceinline__ float min_hi(float x, float hi) { return x > hi ? hi : x; }
+__device__ __forceinline__ uint16_t f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
+__device__ __forceinline__ float f16_val(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+
+// ---------------------------------------------------------------------------
+// reductions in the reference's association orders
+// ---------------------------------------------------------------------------
+template <int N>
+__device__ __forceinline__ float seq_sum(const float* t) {  // parts[0] + parts[1] + ...
+    float s = t[0];
+#pragma unroll
+    for (int i = 1; i < N; i++) s = __fadd_rn(s, t[i]);
+    return s;
+}
+
+template <int N>
+__device__ __forceinline__ float tree_sum(const float* t) {  // adjacent-pair tree
+    float a[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) a[i] = t[i];
+#pragma unroll
+    for (int n = N; n > 1; n >>= 1) {
+#pragma unroll
+        for (int i = 0; i < n / 2; i++) a[i] = __fadd_rn(a[2 * i], a[2 * i + 1]);
+    }
+    return a[0];
+}
+
+// torch CPU float32 `.sum(-1)` over a contiguous dim of 8, 16 or 32
+template <int N>
+__device__ __forceinline__ float torch_sum(const float* t) {
+    float s = 0.0f;
+    if (N == 8) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) s = __fadd_rn(s, t[i]);
+    } else if (N == 16) {
+#pragma unroll
+        for (int l = 0; l < 8; l++) s = __fadd_rn(s, __fadd_rn(t[l], t[8 + l]));
+    } else {
+#pragma unroll
+        for (int l = 0; l < 8; l++)
+            s = __fadd_rn(s, __fadd_rn(__fadd_rn(__fadd_rn(t[l], t[8 + l]), t[16 + l]), t[24 + l]));
+    }
+    return s;
+}
+
+// First index of the largest |x| and the signed value there (absmax_first / argmax).
+template <int N>
+__device__ __forceinline__ void absmax_first(const float* x, float& amax, float& mx) {
+    float a = fabsf(x[0]);
+    float m = x[0];
+#pragma unroll
+    for (int i = 1; i < N; i++) {
+        float v = fabsf(x[i]);
+        if (v > a) { a = v; m = x[i]; }
+    }
+    amax = a;
+    mx = m;
+}
+
+template <int N>
+__device__ __forceinline__ float max_of(const float* x) {
+    float m = x[0];
+#pragma unroll
+    for (int i = 1; i < N; i++) m = x[i] > m ? x[i] : m;
+    return m;
+}
+template <int N>
+__device__ __forceinline__ float min_of(const float* x) {
+    float m = x[0];
+#pragma unroll
+    for (int i = 1; i < N; i++) m = x[i] < m ? x[i] : m;
+    return m;
+}
+
+// torch's `(x*x).sum(-1)` over a 256-element superblock, from squares laid out in
+// shared memory: 32 vectors of 8 lanes, four accumulators over vectors 4i+k, then a
+// left-to-right pass over the 8 lane partials. `lane8` in [0, 8) computes partial
+// `lane8`; the caller reduces the 8 partials with sb_sum256_finish.
+__device__ __forceinline__ float sb_sum256_partial(const float* sq, int lane8) {
+    float acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) a = __fadd_rn(a, sq[8 * (4 * i + k) + lane8]);
+        acc[k] = a;
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
+}
+__device__ __forceinline__ float sb_sum256_finish(const float* part8) {
+    float s = 0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; l++) s = __fadd_rn(s, part8[l]);
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// output staging: copy `nbytes` from shared memory to global with the widest
+// stores the destination alignment allows (16 B body, byte head/tail)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void store_bytes(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src,
+                                            int nbytes, int tid, int nthreads) {
+    int head = (int)((16 - ((uintptr_t)dst & 15)) & 15);
+    if (head > nbytes) head = nbytes;
+    for (int i = tid; i < head; i += nthreads) dst[i] = src[i];
+    int body = (nbytes - head) / 16;
+    uint4* d4 = reinterpret_cast<uint4*>(dst + head);
+    const uint8_t* s = src + head;
+    if (((uintptr_t)s & 3) == 0) {
+        for (int i = tid; i < body; i += nthreads) {
+            const uint32_t* s4 = reinterpret_cast<const uint32_t*>(s + 16 * i);
+            d4[i] = make_uint4(s4[0], s4[1], s4[2], s4[3]);
+        }
+    } else {
+        for (int i = tid; i < body; i += nthreads) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                w[j] = (uint32_t)s[16 * i + 4 * j] | ((uint32_t)s[16 * i + 4 * j + 1] << 8) |
+                       ((uint32_t)s[16 * i + 4 * j + 2] << 16) | ((uint32_t)s[16 * i + 4 * j + 3] << 24);
+            d4[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+    for (int i = head + 16 * body + tid; i < nbytes; i += nthreads) dst[i] = src[i];
+}
+
+// Parameters shared by every quantize launch.
+struct QuantArgs {
+    const void* src;      // n_rows x k elements of src_type, row-major, contiguous
+    int src_type;
+    int64_t n_rows, k;
+    const float* qw;      // k importance weights or nullptr
+    uint8_t* dst;         // n_rows rows of dst_row_bytes
+    int64_t dst_row_bytes;
+    int64_t row_bytes;    // packed bytes per row
+    int64_t nblk;         // total quant blocks (superblocks, or 32-blocks for Q4_0)
+    int64_t nblk_row;     // blocks per row
+};
+
+// Copy the packed output of blocks [b0, b0 + nb) from shared memory to the rows
+// they belong to; rows may be strided in the destination.
+__device__ __forceinline__ void store_tile(const QuantArgs& a, const uint8_t* stage, int64_t b0, int nb,
+                                           int block_bytes, int tid, int nthreads) {
+    int64_t b = b0;
+    int done = 0;
+    while (done < nb) {
+        int64_t row = b / a.nblk_row, col = b - row * a.nblk_row;
+        int run = (int)min((int64_t)(nb - done), a.nblk_row - col);
+        if (a.dst_row_bytes == a.row_bytes) run = nb - done;  // contiguous rows: one run
+        uint8_t* d = a.dst + row * a.dst_row_bytes + col * block_bytes;
+        store_bytes(d, stage + (size_t)done * block_bytes, run * block_bytes, tid, nthreads);
+        done += run;
+        b += run;
+    }
+}
+
+}  // namespace qs

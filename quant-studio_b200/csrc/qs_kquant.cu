@@ -1,0 +1,601 @@
+// K-quant (Q2_K..Q6_K), IQ4_XS and Q4_0 kernels for sm_100a.
+//
+// Layout: one thread per quantization group (16 or 32 values in registers), the
+// threads of a superblock are consecutive lanes of one warp, a CTA of 256 threads
+// works on a tile of 16 or 32 superblocks and stages the packed tile in shared
+// memory before a coalesced store. Reference for every formula: the eager torch path
+// of ngxson/quant-studio kernels/<type>.py (citations per kernel).
+#include "qs_kquant.cuh"
+#include "qs_kernels.h"
+
+namespace qs {
+
+// ---------------------------------------------------------------------------
+// Q4_0 (kernels/q4_0.py:14-33): one thread per 32-block, HBM-bound
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) q4_0_kernel(QuantArgs a) {
+    constexpr int BB = 18;
+    __shared__ __align__(16) uint8_t s_out[256 * BB];
+    const int tid = threadIdx.x;
+    for (int64_t tile = blockIdx.x; tile * 256 < a.nblk; tile += gridDim.x) {
+        const int64_t b = tile * 256 + tid;
+        const int nvalid = (int)min((int64_t)256, a.nblk - tile * 256);
+        if (tid < nvalid) {
+            float x[32], amax, mx;
+            load_row<32>(a.src, b * 32, a.src_type, x);
+            absmax_first<32>(x, amax, mx);
+            const float d = __fdiv_rn(mx, -8.0f);
+            const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
+            uint8_t* o = s_out + tid * BB;
+            const uint16_t dh = f16_bits(d);
+            o[0] = (uint8_t)dh;
+            o[1] = (uint8_t)(dh >> 8);
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                int lo = (int)clampf(floorf(x[i] * id + 8.5f), 0.0f, 15.0f);
+                int hi = (int)clampf(floorf(x[16 + i] * id + 8.5f), 0.0f, 15.0f);
+                o[2 + i] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+        __syncthreads();
+        store_tile(a, s_out, tile * 256, nvalid, BB, tid, 256);
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q2_K / Q4_K / Q5_K (kernels/q2_k.py:25-81, q4_k.py:25-79, q5_k.py:25-82)
+// ---------------------------------------------------------------------------
+template <int T>
+struct QkxTraits;
+template <>
+struct QkxTraits<QS_Q2_K> { static constexpr int GS = 16, NMAX = 3, BB = 84, QPMAX = 15; static constexpr float SIGFAC = 1.0f; };
+template <>
+struct QkxTraits<QS_Q4_K> { static constexpr int GS = 32, NMAX = 15, BB = 144, QPMAX = 63; static constexpr float SIGFAC = 2.0f; };
+template <>
+struct QkxTraits<QS_Q5_K> { static constexpr int GS = 32, NMAX = 31, BB = 176, QPMAX = 63; static constexpr float SIGFAC = 2.0f; };
+
+template <int T, bool IMAT>
+__global__ void __launch_bounds__(256) qkx_kernel(QuantArgs a, KParams p) {
+    using Tr = QkxTraits<T>;
+    constexpr int GS = Tr::GS, NG = QK_K / GS, SBT = 256 / NG, BB = Tr::BB;
+    constexpr bool MAD = (T == QS_Q2_K) && !IMAT;
+    __shared__ float s_steps[40], s_qp[8];
+    __shared__ __align__(16) float s_sq[SBT * QK_K];  // squares, then the SB's level bytes
+    __shared__ float s_part[SBT][8];
+    __shared__ float s_sc[SBT][NG], s_mn[SBT][NG], s_sw[SBT][NG], s_ls[SBT][NG], s_lm[SBT][NG];
+    __shared__ float s_d[SBT], s_m[SBT];
+    __shared__ __align__(16) uint8_t s_out[SBT * BB];
+
+    const int tid = threadIdx.x, sbl = tid / NG, g = tid % NG;
+    if (tid < 40) s_steps[tid] = p.steps[tid];
+    if (tid < 8) s_qp[tid] = p.qp[tid];
+    __syncthreads();
+    float* sq = s_sq + sbl * QK_K;
+    uint8_t* lev = reinterpret_cast<uint8_t*>(sq);
+
+    for (int64_t tile = blockIdx.x; tile * SBT < a.nblk; tile += gridDim.x) {
+        const int64_t b = min(tile * SBT + sbl, a.nblk - 1);  // tail lanes redo the last block
+        float x[GS], w[GS], L[GS];
+        load_row<GS>(a.src, b * QK_K + g * GS, a.src_type, x);
+        if (IMAT) {
+#pragma unroll
+            for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
+            __syncwarp();
+            if (g < 8) s_part[sbl][g] = sb_sum256_partial(sq, g);
+            __syncwarp();
+            const float sigma2 = __fdiv_rn(Tr::SIGFAC * sb_sum256_finish(s_part[sbl]), 256.0f);
+            float q[GS];
+            load_f32<GS>(a.qw + (b % a.nblk_row) * QK_K + g * GS, q);
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = q[i] * sqrtf(sigma2 + x[i] * x[i]);
+        } else if (T == QS_Q2_K) {
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = fabsf(x[i]);
+        } else {
+            float t[GS];
+#pragma unroll
+            for (int i = 0; i < GS; i++) t[i] = x[i] * x[i];
+            const float av_x = sqrtf(__fdiv_rn(torch_sum<GS>(t), 32.0f));
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = av_x + fabsf(x[i]);
+        }
+        float the_min;
+        const float scale = qkx_search<GS, Tr::NMAX, MAD>(x, w, s_steps, p.nsteps, the_min, L);
+        s_sc[sbl][g] = scale;
+        s_mn[sbl][g] = the_min;
+        if (IMAT) s_sw[sbl][g] = torch_sum<GS>(w);
+        __syncwarp();
+
+        // superblock scale/min quantization
+        uint16_t d16, m16;
+        int ls, lm;  // this group's 8-bit codes
+        if (IMAT) {
+            if (g < 2) {
+                float v[NG], sw[NG], lv[NG];
+#pragma unroll
+                for (int j = 0; j < NG; j++) {
+                    v[j] = g == 0 ? s_sc[sbl][j] : s_mn[sbl][j];
+                    sw[j] = s_sw[sbl][j];
+                }
+                const float dd = qp_search<NG>(v, sw, (float)Tr::QPMAX, s_qp, lv);
+#pragma unroll
+                for (int j = 0; j < NG; j++) (g == 0 ? s_ls : s_lm)[sbl][j] = lv[j];
+                (g == 0 ? s_d : s_m)[sbl] = dd;
+            }
+            __syncwarp();
+            d16 = f16_bits(s_d[sbl]);
+            m16 = f16_bits(s_m[sbl]);
+            ls = (int)((long long)s_ls[sbl][g] & 0xFF);
+            lm = (int)((long long)s_lm[sbl][g] & 0xFF);
+        } else {
+            float max_scale = s_sc[sbl][0], max_min = s_mn[sbl][0];
+#pragma unroll
+            for (int j = 1; j < NG; j++) {
+                max_scale = s_sc[sbl][j] > max_scale ? s_sc[sbl][j] : max_scale;
+                max_min = s_mn[sbl][j] > max_min ? s_mn[sbl][j] : max_min;
+            }
+            if (T == QS_Q2_K) {
+                const float inv_s = max_scale > 0.0f ? __fdiv_rn(15.0f, max_scale) : 0.0f;
+                const float inv_m = max_min > 0.0f ? __fdiv_rn(15.0f, max_min) : 0.0f;
+                ls = (int)((long long)rintf(inv_s * scale) & 0xFF);
+                lm = (int)((long long)rintf(inv_m * the_min) & 0xFF);
+                d16 = f16_bits(max_scale > 0.0f ? __fdiv_rn(max_scale, 15.0f) : 0.0f);
+                m16 = f16_bits(max_min > 0.0f ? __fdiv_rn(max_min, 15.0f) : 0.0f);
+            } else {
+                const float inv_s = max_scale > 0.0f ? rcp_rn(max_scale) * 63.0f : 0.0f;
+                const float inv_m = max_min > 0.0f ? rcp_rn(max_min) * 63.0f : 0.0f;
+                ls = min((int)((long long)rintf(inv_s * scale) & 0xFF), 63);
+                lm = min((int)((long long)rintf(inv_m * the_min) & 0xFF), 63);
+                d16 = f16_bits(__fdiv_rn(max_scale, 63.0f));
+                m16 = f16_bits(__fdiv_rn(max_min, 63.0f));
+            }
+            s_ls[sbl][g] = (float)ls;
+            s_lm[sbl][g] = (float)lm;
+        }
+
+        // requantize with the stored block scales; d == 0 keeps the search levels
+        int scb = 0;
+        float dg, mg;
+        if (T == QS_Q2_K) {
+            scb = (ls | (lm << 4)) & 0xFF;
+            dg = f16_val(d16) * (float)(scb & 0xF);
+            mg = f16_val(m16) * (float)(scb >> 4);
+        } else {
+            dg = f16_val(d16) * (float)(ls & 63);
+            mg = f16_val(m16) * (float)(lm & 63);
+        }
+#pragma unroll
+        for (int i = 0; i < GS; i++) {
+            const float q = dg != 0.0f ? clampf(rintf(__fdiv_rn(x[i] + mg, dg)), 0.0f, (float)Tr::NMAX) : L[i];
+            lev[g * GS + i] = (uint8_t)(int)q;
+        }
+        __syncwarp();
+
+        uint8_t* o = s_out + sbl * BB;
+        if (T == QS_Q2_K) {
+            o[g] = (uint8_t)scb;
+#pragma unroll
+            for (int i = 4 * g; i < 4 * g + 4; i++) {
+                const int h = i >> 5, l = i & 31;
+                const uint8_t* q = lev + 128 * h + l;
+                o[16 + i] = (uint8_t)(q[0] | (q[32] << 2) | (q[64] << 4) | (q[96] << 6));
+            }
+            if (g == 0) {
+                o[80] = (uint8_t)d16; o[81] = (uint8_t)(d16 >> 8);
+                o[82] = (uint8_t)m16; o[83] = (uint8_t)(m16 >> 8);
+            }
+        } else {
+            if (g == 0) {
+                o[0] = (uint8_t)d16; o[1] = (uint8_t)(d16 >> 8);
+                o[2] = (uint8_t)m16; o[3] = (uint8_t)(m16 >> 8);
+            }
+            if (g < 4) {
+                const int l0 = (int)s_ls[sbl][g], l4 = (int)s_ls[sbl][4 + g];
+                const int m0 = (int)s_lm[sbl][g], m4 = (int)s_lm[sbl][4 + g];
+                o[4 + g] = (uint8_t)(l0 | ((l4 >> 4) << 6));
+                o[8 + g] = (uint8_t)(m0 | ((m4 >> 4) << 6));
+                o[12 + g] = (uint8_t)((l4 & 0xF) | ((m4 & 0xF) << 4));
+            }
+            int qs0 = 16;
+            if (T == QS_Q5_K) {
+                qs0 = 48;
+#pragma unroll
+                for (int l = 4 * g; l < 4 * g + 4; l++) {
+                    int v = 0;
+#pragma unroll
+                    for (int s = 0; s < 8; s++) v += (lev[32 * s + l] >> 4) << s;
+                    o[16 + l] = (uint8_t)v;
+                }
+            }
+            const int j = g >> 1, l0 = 16 * (g & 1);
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const uint8_t* q = lev + 64 * j + l0 + i;
+                o[qs0 + 16 * g + i] = (uint8_t)((q[0] & 0xF) | ((q[32] & 0xF) << 4));
+            }
+        }
+        __syncthreads();
+        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, 256);
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Q6_K / Q3_K (kernels/q6_k.py:22-65, q3_k.py:23-78): one thread per 16-group
+// ---------------------------------------------------------------------------
+template <int T, bool IMAT>
+__global__ void __launch_bounds__(256) qx_kernel(QuantArgs a, KParams p) {
+    constexpr int GS = 16, NG = 16, SBT = 16;
+    constexpr int BB = T == QS_Q6_K ? 210 : 110;
+    __shared__ float s_qx[18], s_qx2[18];
+    __shared__ __align__(16) float s_sq[SBT * QK_K];
+    __shared__ float s_sc[SBT][NG], s_sw[SBT][NG], s_ls[SBT][NG];
+    __shared__ float s_d[SBT], s_sig[SBT];
+    __shared__ __align__(16) uint8_t s_out[SBT * BB];
+
+    const int tid = threadIdx.x, sbl = tid / NG, g = tid % NG;
+    if (tid < 18) { s_qx[tid] = p.qx[tid]; s_qx2[tid] = p.qx2[tid]; }
+    __syncthreads();
+    float* sq = s_sq + sbl * QK_K;
+    uint8_t* lev = reinterpret_cast<uint8_t*>(sq);
+
+    for (int64_t tile = blockIdx.x; tile * SBT < a.nblk; tile += gridDim.x) {
+        const int64_t b = min(tile * SBT + sbl, a.nblk - 1);
+        float x[GS], w[GS], L[GS];
+        load_row<GS>(a.src, b * QK_K + g * GS, a.src_type, x);
+        const float* qwp = IMAT ? a.qw + (b % a.nblk_row) * QK_K + g * GS : nullptr;
+        float scale;
+        if (T == QS_Q6_K) {
+            if (IMAT) load_f32<GS>(qwp, w);
+            else {
+#pragma unroll
+                for (int i = 0; i < GS; i++) w[i] = x[i] * x[i];
+            }
+            scale = qx_search<GS>(x, w, 32.0f, s_qx, L);
+        } else if (!IMAT) {
+            scale = q3_search<GS>(x, 4.0f, L);
+        } else {
+            // sigma2 = 2 * seq_sum(x*x over 256) / 256: one strict left-to-right chain
+#pragma unroll
+            for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
+            __syncwarp();
+            if (g == 0) {
+                float s = sq[0];
+                for (int i = 1; i < QK_K; i++) s = __fadd_rn(s, sq[i]);
+                s_sig[sbl] = __fdiv_rn(2.0f * s, 256.0f);
+            }
+            __syncwarp();
+            const float sigma2 = s_sig[sbl];
+            float q[GS];
+            load_f32<GS>(qwp, q);
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = q[i] * sqrtf(sigma2 + x[i] * x[i]);
+            scale = qx_search<GS>(x, w, 4.0f, s_qx, L);
+            s_sw[sbl][g] = seq_sum<GS>(w);
+        }
+        s_sc[sbl][g] = scale;
+        __syncwarp();
+
+        float sc16[NG];
+#pragma unroll
+        for (int j = 0; j < NG; j++) sc16[j] = s_sc[sbl][j];
+        uint16_t d16;
+        int myls;
+        bool live = true;
+        if (T == QS_Q6_K) {
+            float amax, max_scale;
+            absmax_first<NG>(sc16, amax, max_scale);
+            live = amax >= EPS15;
+            const float iscale = rcp_rn(live ? max_scale : 1.0f) * -128.0f;
+            d16 = f16_bits(live ? rcp_rn(iscale) : 0.0f);
+            long long v = (long long)min_hi(rintf(iscale * scale), 127.0f);
+            v = ((v & 0xFF) ^ 0x80) - 0x80;
+            myls = live ? (int)v : 0;
+        } else if (!IMAT) {
+            float amax, max_scale;
+            absmax_first<NG>(sc16, amax, max_scale);
+            const bool has = max_scale != 0.0f;
+            const float iscale = rcp_rn(has ? max_scale : 1.0f) * -32.0f;
+            long long l = (long long)rintf(iscale * scale);
+            l = ((l & 0xFF) ^ 0x80) - 0x80;
+            l = l < -32 ? -32 : (l > 31 ? 31 : l);
+            myls = has ? (int)(l + 32) : 0;
+            d16 = f16_bits(has ? rcp_rn(iscale) : 0.0f);
+        } else {
+            if (g == 0) {
+                float sw[NG], lv[NG];
+#pragma unroll
+                for (int j = 0; j < NG; j++) sw[j] = s_sw[sbl][j];
+                s_d[sbl] = qx_search<NG>(sc16, sw, 32.0f, s_qx2, lv);
+#pragma unroll
+                for (int j = 0; j < NG; j++) s_ls[sbl][j] = lv[j];
+            }
+            __syncwarp();
+            d16 = f16_bits(s_d[sbl]);
+            myls = (int)s_ls[sbl][g];
+        }
+        s_ls[sbl][g] = (float)myls;
+        __syncwarp();
+
+        const float dd = f16_val(d16);
+        if (T == QS_Q6_K) {
+            const float dq = dd * (float)myls;
+#pragma unroll
+            for (int i = 0; i < GS; i++) {
+                const float v = dq != 0.0f ? clampf(rintf(__fdiv_rn(x[i], dq)), -32.0f, 31.0f) + 32.0f : L[i];
+                lev[g * GS + i] = live ? (uint8_t)(int)v : 0;
+            }
+        } else {
+            const float dq = dd * (float)(myls - 32);
+#pragma unroll
+            for (int i = 0; i < GS; i++) {
+                const float v = dq != 0.0f ? clampf(rintf(__fdiv_rn(x[i], dq)), -4.0f, 3.0f) + 4.0f : L[i];
+                lev[g * GS + i] = (uint8_t)(int)v;
+            }
+        }
+        __syncwarp();
+
+        uint8_t* o = s_out + sbl * BB;
+        if (T == QS_Q6_K) {
+#pragma unroll
+            for (int i = 8 * g; i < 8 * g + 8; i++) {  // ql
+                const int h = i >> 6, r = i & 63, l = r & 31, hi = r >> 5;
+                const uint8_t* q = lev + 128 * h + 32 * hi + l;
+                o[i] = (uint8_t)((q[0] & 0xF) | ((q[64] & 0xF) << 4));
+            }
+#pragma unroll
+            for (int i = 4 * g; i < 4 * g + 4; i++) {  // qh
+                const int h = i >> 5, l = i & 31;
+                const uint8_t* q = lev + 128 * h + l;
+                o[128 + i] = (uint8_t)((q[0] >> 4) | ((q[32] >> 4) << 2) | ((q[64] >> 4) << 4) | ((q[96] >> 4) << 6));
+            }
+            o[192 + g] = (uint8_t)(int8_t)myls;
+            if (g == 0) { o[208] = (uint8_t)d16; o[209] = (uint8_t)(d16 >> 8); }
+        } else {
+#pragma unroll
+            for (int l = 2 * g; l < 2 * g + 2; l++) {  // hmask
+                int v = 0;
+#pragma unroll
+                for (int bb = 0; bb < 8; bb++) v |= (lev[32 * bb + l] > 3) << bb;
+                o[l] = (uint8_t)v;
+            }
+#pragma unroll
+            for (int i = 4 * g; i < 4 * g + 4; i++) {  // qs
+                const int h = i >> 5, l = i & 31;
+                int v = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    int q = lev[128 * h + 32 * j + l];
+                    v |= (q > 3 ? q - 4 : q) << (2 * j);
+                }
+                o[32 + i] = (uint8_t)v;
+            }
+            if (g < 8) {
+                const int a0 = (int)s_ls[sbl][g], a8 = (int)s_ls[sbl][g + 8];
+                o[96 + g] = (uint8_t)((a0 & 0xF) | ((a8 & 0xF) << 4));
+            }
+            if (g < 4) {
+                int v = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) v |= ((int)s_ls[sbl][4 * j + g] >> 4) << (2 * j);
+                o[104 + g] = (uint8_t)v;
+            }
+            if (g == 0) { o[108] = (uint8_t)d16; o[109] = (uint8_t)(d16 >> 8); }
+        }
+        __syncthreads();
+        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, 256);
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// IQ4_XS (kernels/iq4_xs.py:35-188): one thread per 32-block
+// ---------------------------------------------------------------------------
+__constant__ float c_kv_iq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+// _best_index (iq4_xs.py:35-39): bracket with searchsorted(right), midpoint compare
+__device__ __forceinline__ int iq4nl_index(const float* kv, float al) {
+    int p = 0;  // number of kv[1..14] <= al
+#pragma unroll
+    for (int step = 8; step >= 1; step >>= 1)
+        if (p + step <= 14 && kv[p + step] <= al) p += step;
+    const int mu = 1 + p;
+    return (al - kv[mu - 1] < kv[mu] - al) ? mu - 1 : mu;
+}
+
+template <bool IMAT>
+__global__ void __launch_bounds__(256) iq4xs_kernel(QuantArgs a) {
+    constexpr int GS = 32, NG = 8, SBT = 32, BB = 136;
+    __shared__ float s_kv[16];
+    __shared__ __align__(16) float s_sq[SBT * QK_K];
+    __shared__ float s_part[SBT][8], s_sc[SBT][NG];
+    __shared__ __align__(16) uint8_t s_out[SBT * BB];
+    const int tid = threadIdx.x, sbl = tid / NG, g = tid % NG;
+    if (tid < 16) s_kv[tid] = c_kv_iq4nl[tid];
+    __syncthreads();
+    float* sq = s_sq + sbl * QK_K;
+
+    for (int64_t tile = blockIdx.x; tile * SBT < a.nblk; tile += gridDim.x) {
+        const int64_t b = min(tile * SBT + sbl, a.nblk - 1);
+        float x[GS], w[GS], t[GS];
+        load_row<GS>(a.src, b * QK_K + g * GS, a.src_type, x);
+        if (IMAT) {
+#pragma unroll
+            for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
+            __syncwarp();
+            if (g < 8) s_part[sbl][g] = sb_sum256_partial(sq, g);
+            __syncwarp();
+            const float sigma2 = __fdiv_rn(2.0f * sb_sum256_finish(s_part[sbl]), 256.0f);
+            float q[GS];
+            load_f32<GS>(a.qw + (b % a.nblk_row) * QK_K + g * GS, q);
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = q[i] * sqrtf(sigma2 + x[i] * x[i]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = x[i] * x[i];
+        }
+        // _search_scales_eager (iq4_xs.py:52-76)
+        float amax, mx;
+        absmax_first<GS>(x, amax, mx);
+        const bool live = fabsf(mx) >= EPS15;
+        const float mxs = live ? mx : 1.0f;
+        const float d0 = __fdiv_rn(-mxs, -127.0f);
+        const float id0 = rcp_rn(d0);
+        float sumqx, sumq2;
+        {
+            float u[GS];
+#pragma unroll
+            for (int i = 0; i < GS; i++) {
+                const float q = s_kv[iq4nl_index(s_kv, id0 * x[i])];
+                t[i] = (w[i] * q) * x[i];
+                u[i] = (w[i] * q) * q;
+            }
+            sumqx = seq_sum<GS>(t);
+            sumq2 = seq_sum<GS>(u);
+        }
+        float d = sumq2 > 0.0f ? __fdiv_rn(sumqx, sumq2) : 0.0f;
+        float best = d * sumqx;
+        const float r = rcp_rn(mxs);
+#pragma unroll 1
+        for (int itry = -7; itry <= 7; itry++) {
+            const float idv = r * (float)(itry - 127);
+            float sx = 0.0f, s2 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < GS; i++) {
+                const float q = s_kv[iq4nl_index(s_kv, idv * x[i])];
+                const float wq = w[i] * q;
+                sx = i == 0 ? wq * x[i] : sx + wq * x[i];
+                s2 = i == 0 ? wq * q : s2 + wq * q;
+            }
+            if (s2 > 0.0f && sx * sx > best * s2) {
+                const float nd = __fdiv_rn(sx, s2);
+                d = nd;
+                best = nd * sx;
+            }
+        }
+        const float scale = live ? d : 0.0f;
+        s_sc[sbl][g] = scale;
+        __syncwarp();
+
+        float sc8[NG], as, max_scale;
+#pragma unroll
+        for (int j = 0; j < NG; j++) sc8[j] = s_sc[sbl][j];
+        absmax_first<NG>(sc8, as, max_scale);
+        const float dsb = __fdiv_rn(-max_scale, 32.0f);
+        const float idq = dsb != 0.0f ? rcp_rn(dsb) : 0.0f;
+        uint8_t* o = s_out + sbl * BB;
+        {
+            const float ls = clampf(rintf(idq * scale), -32.0f, 31.0f);
+            const float dl = dsb * ls;
+            const float idl = dl != 0.0f ? rcp_rn(dl) : 0.0f;
+#pragma unroll
+            for (int l = 0; l < 16; l++) {
+                const int lo = iq4nl_index(s_kv, idl * x[l]);
+                const int hi = iq4nl_index(s_kv, idl * x[16 + l]);
+                o[8 + 16 * g + l] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+        if (g == 0) {
+            int lsq[NG], hb = 0;
+#pragma unroll
+            for (int j = 0; j < NG; j++) lsq[j] = (int)(clampf(rintf(idq * sc8[j]), -32.0f, 31.0f) + 32.0f);
+#pragma unroll
+            for (int j = 0; j < NG; j++) hb += (lsq[j] >> 4) << (2 * j);
+            const uint16_t dh = f16_bits(dsb);
+            o[0] = (uint8_t)dh; o[1] = (uint8_t)(dh >> 8);
+            o[2] = (uint8_t)(hb & 0xFF); o[3] = (uint8_t)(hb >> 8);
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[4 + j] = (uint8_t)((lsq[2 * j] & 0xF) | ((lsq[2 * j + 1] & 0xF) << 4));
+        }
+        __syncthreads();
+        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, 256);
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side: candidate tables folded exactly like the reference's numpy/python
+// expressions (host code is built with -ffp-contract=off), grid sizing, launch
+// ---------------------------------------------------------------------------
+static void qkx_steps(float rmin, float rdelta, int nstep, int nmax, KParams& p) {  // kq_common.py:21-24
+    for (int s = 0; s <= nstep; s++) p.steps[s] = (rmin + rdelta * (float)s) + (float)nmax;
+    p.nsteps = nstep + 1;
+}
+static void qp_steps(int nmax, KParams& p) {  // kq_common.py:27-30
+    int j = 0;
+    for (int s = -4; s <= 4; s++) if (s) p.qp[j++] = 0.1f * (float)s + (float)nmax;
+}
+static void qx_steps(int nmax, float* c) {  // qx_common.py:20-23
+    int j = 0;
+    for (int s = -9; s <= 9; s++) if (s) c[j++] = (float)nmax + 0.1f * (float)s;
+}
+
+template <typename K>
+static int grid_for(K kernel, int64_t tiles, const LaunchCtx& ctx) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+    int64_t g = (int64_t)per_sm * ctx.num_sms;
+    return (int)(tiles < g ? (tiles > 0 ? tiles : 1) : g);
+}
+
+cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
+    KParams p;
+    memset(&p, 0, sizeof(p));
+    const bool imat = a.qw != nullptr;
+    cudaStream_t st = ctx.stream;
+    switch (type) {
+    case QS_Q4_0: {
+        auto k = q4_0_kernel;
+        q4_0_kernel<<<grid_for(k, (a.nblk + 255) / 256, ctx), 256, 0, st>>>(a);
+        break;
+    }
+    case QS_Q4_K:
+    case QS_Q5_K:
+    case QS_Q2_K: {
+        const int nmax = type == QS_Q4_K ? 15 : (type == QS_Q5_K ? 31 : 3);
+        if (imat) qkx_steps(-0.9f, 0.05f, 36, nmax, p);
+        else if (type == QS_Q4_K) qkx_steps(-1.0f, 0.1f, 20, 15, p);
+        else qkx_steps(-0.5f, 0.1f, 15, nmax, p);
+        qp_steps(type == QS_Q2_K ? 15 : 63, p);
+        const int sbt = type == QS_Q2_K ? 16 : 32;
+        const int64_t tiles = (a.nblk + sbt - 1) / sbt;
+#define QS_LAUNCH_QKX(T, I)                                            \
+    {                                                                  \
+        auto k = qkx_kernel<T, I>;                                     \
+        qkx_kernel<T, I><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a, p); \
+    }
+        if (type == QS_Q4_K) { if (imat) QS_LAUNCH_QKX(QS_Q4_K, true) else QS_LAUNCH_QKX(QS_Q4_K, false) }
+        else if (type == QS_Q5_K) { if (imat) QS_LAUNCH_QKX(QS_Q5_K, true) else QS_LAUNCH_QKX(QS_Q5_K, false) }
+        else { if (imat) QS_LAUNCH_QKX(QS_Q2_K, true) else QS_LAUNCH_QKX(QS_Q2_K, false) }
+#undef QS_LAUNCH_QKX
+        break;
+    }
+    case QS_Q6_K:
+    case QS_Q3_K: {
+        qx_steps(type == QS_Q6_K ? 32 : 4, p.qx);
+        qx_steps(32, p.qx2);
+        const int64_t tiles = (a.nblk + 15) / 16;
+#define QS_LAUNCH_QX(T, I)                                            \
+    {                                                                 \
+        auto k = qx_kernel<T, I>;                                     \
+        qx_kernel<T, I><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a, p); \
+    }
+        if (type == QS_Q6_K) { if (imat) QS_LAUNCH_QX(QS_Q6_K, true) else QS_LAUNCH_QX(QS_Q6_K, false) }
+        else { if (imat) QS_LAUNCH_QX(QS_Q3_K, true) else QS_LAUNCH_QX(QS_Q3_K, false) }
+#undef QS_LAUNCH_QX
+        break;
+    }
+    case QS_IQ4_XS: {
+        const int64_t tiles = (a.nblk + 31) / 32;
+        if (imat) { auto k = iq4xs_kernel<true>; iq4xs_kernel<true><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a); }
+        else { auto k = iq4xs_kernel<false>; iq4xs_kernel<false><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a); }
+        break;
+    }
+    default:
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace qs

@@ -1,0 +1,110 @@
+"""libqsb200 on a CUDA device against the oracle and the reference's fixtures.
+
+Bit-exact is the bar for every type: the kernels restate the reference's eager path with
+IEEE arithmetic, so their bytes equal the oracle's and the reference-with-IEEE-sqrt
+fixtures exactly."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden_cases, golden_x
+from kernels import _native
+
+pytestmark = pytest.mark.gpu
+
+GT = oracle.TYPE_IDS
+GPU_TYPES = ["q4_0", "q2_k", "q3_k", "q4_k", "q5_k", "q6_k", "iq4_xs"]
+
+
+def dev_input(inputs, src):
+    """The fixture input in its stored dtype, on cuda:0."""
+    if src == "A":
+        return torch.from_numpy(inputs["A_bf16"].view(np.int16).copy()).view(torch.bfloat16).cuda()
+    if src == "B":
+        return torch.from_numpy(inputs["B_f32"].copy()).cuda()
+    return torch.from_numpy(inputs["C_f16"].copy()).cuda()
+
+
+def synth(rows, k, seed, dtype=torch.bfloat16):
+    """N(0, 0.02) with 0.1 % N(0, 0.5) outliers, the benchmark distribution."""
+    rng = np.random.default_rng(seed)
+    a = rng.normal(0.0, 0.02, (rows, k))
+    m = rng.random(a.shape) < 0.001
+    a[m] = rng.normal(0.0, 0.5, int(m.sum()))
+    t = torch.from_numpy(a.astype(np.float32)).to(dtype)
+    qw = rng.lognormal(0.0, 1.5, k).astype(np.float32)
+    return t, qw
+
+
+def run(qtype, x, qw=None):
+    q = None if qw is None else torch.from_numpy(np.ascontiguousarray(qw)).cuda()
+    out = _native.quantize(GT[qtype], x.cuda(), q)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("qtype", GPU_TYPES)
+def test_golden_fixtures_bit_exact(qtype, inputs):
+    for key, src, qwk, _ref, ref_ieee in golden_cases(qtype):
+        got = run(qtype, dev_input(inputs, src), None if qwk is None else inputs[qwk])
+        bad = np.nonzero((got != ref_ieee).any(1))[0]
+        assert bad.size == 0, f"{qtype} {key}: rows {bad[:8]} differ from the reference"
+
+
+@pytest.mark.parametrize("qtype", GPU_TYPES)
+def test_matches_oracle_on_benchmark_distribution(qtype):
+    x, qw = synth(512, 4096, seed=11)
+    xf = x.float().numpy()
+    for q in ((qw,) if oracle.TYPE_IDS[qtype] in (16, 17, 22) else (None, qw)):
+        got = run(qtype, x, q)
+        ref = oracle.quantize(qtype, xf, q)
+        bad = np.nonzero((got != ref).any(1))[0]
+        assert bad.size == 0, f"{qtype} qw={q is not None}: rows {bad[:8]} differ"
+
+
+@pytest.mark.parametrize("qtype", GPU_TYPES)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_other_source_dtypes(qtype, dtype):
+    x, qw = synth(37, 1024, seed=5, dtype=dtype)
+    q = qw if oracle.TYPE_IDS[qtype] in (16, 17, 22) else None
+    assert np.array_equal(run(qtype, x, q), oracle.quantize(qtype, x.float().numpy(), q))
+
+
+@pytest.mark.parametrize("qtype", GPU_TYPES)
+def test_strided_destination_and_every_byte_written(qtype):
+    """Rows land at dst_row_bytes strides; padding bytes stay untouched, packed bytes all written."""
+    x, qw = synth(45, 512, seed=3)
+    q = torch.from_numpy(qw).cuda()
+    rb = _native.row_bytes(GT[qtype], 512)
+    buf = torch.full((45, rb + 13), 0xAB, dtype=torch.uint8, device="cuda")
+    _native.quantize_into(GT[qtype], x.cuda(), q, buf[:, :rb])
+    torch.cuda.synchronize()
+    got = buf.cpu().numpy()
+    assert np.all(got[:, rb:] == 0xAB)
+    assert np.array_equal(got[:, :rb], oracle.quantize(qtype, x.float().numpy(), qw))
+
+
+@pytest.mark.parametrize("qtype", GPU_TYPES)
+def test_chunking_and_stream_invariance(qtype):
+    """Bytes do not depend on how rows are split into launches or on the stream used."""
+    x, qw = synth(300, 768, seed=9)
+    q = torch.from_numpy(qw).cuda()
+    xd = x.cuda()
+    whole = _native.quantize(GT[qtype], xd, q)
+    s = torch.cuda.Stream()
+    parts = []
+    with torch.cuda.stream(s):
+        for r0 in range(0, 300, 77):
+            parts.append(_native.quantize(GT[qtype], xd[r0:r0 + 77], q))
+    s.synchronize()
+    assert torch.equal(torch.cat(parts), whole)
+
+
+def test_tiny_and_single_block_inputs():
+    for qtype in GPU_TYPES:
+        k = 32 if qtype == "q4_0" else 256
+        for rows in (1, 2, 3):
+            x, qw = synth(rows, k, seed=rows)
+            assert np.array_equal(run(qtype, x, qw), oracle.quantize(qtype, x.float().numpy(), qw)), qtype
