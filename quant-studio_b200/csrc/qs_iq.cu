@@ -1,19 +1,673 @@
 // IQ2_XXS / IQ2_XS / IQ2_S / IQ3_XXS / IQ3_S lattice-search kernels (sm_100a).
+//
+// Reference: kernels/iq2.py:418-498 (IQ2_XXS), kernels/iq2xs_common.py:280-355 with
+// iq2_xs.py:20-69 / iq2_s.py:21-62, kernels/iq3_xxs.py:31-134, kernels/iq3_s.py:31-140.
+//
+// Mapping. One thread per quantization group (16 or 32 values, in registers) runs the
+// weights, the sign handling and the accept chain over the candidate scales. The grid
+// projections are where the time goes: a subgroup's tentative code is either on the
+// lattice (one table lookup) or needs a best-neighbour search over a list of 1..292
+// candidates. Lists are that uneven, so one lane per search would leave most of a warp
+// idle. Instead each warp queues its off-grid searches in shared memory (all sweep steps
+// of a batch at once: their codes depend only on the group maximum) and walks the
+// concatenated candidate stream in 32 equal slices, one per lane. A lane keeps the best
+// (d2, position) of each list it touches and merges it into the list's result with a
+// 64-bit atomicMin, which keeps the reference's first-minimum rule (strict <).
+// The weighted distance of one candidate is a sum over positions of terms that depend
+// only on the position and the candidate's level there, so each lane first tabulates
+// the 4 x 8 (IQ2) or 8 x 4 (IQ3) terms of its current search, computed exactly as the
+// reference does, and then reads them per candidate.
+#include <algorithm>
+#include <vector>
+
+#include "iq_grids.h"
+#include "qs_kquant.cuh"
 #include "qs_kernels.h"
 
 namespace qs {
 
-struct IqTables {
-    int dummy;
+// ---------------------------------------------------------------------------
+// device tables
+// ---------------------------------------------------------------------------
+struct IqGridDev {
+    const uint16_t* kgrid;  // grid index -> code
+    const uint32_t* nbr;    // code index -> 0x80000000 | grid index (on grid) or off << 9 | len
+    const uint16_t* list;   // neighbour lists (grid indices), (distance, index) order
+    int grid;
 };
 
+struct IqTables {
+    IqGridDev g[5];
+    void* mem = nullptr;
+};
+
+enum { G_IQ2XXS = 0, G_IQ2XS, G_IQ2S, G_IQ3XXS, G_IQ3S };
+
+// Neighbour lists of every reachable off-grid code (the reference's Tables classes:
+// iq2.py:31-74, iq2xs_common.py:41-95, iq3_common.py:29-68). IQ2 codes are indexed in
+// base 3 because sweep levels are clamped to 0..2, IQ3 codes directly (levels 0..7).
+static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwant, std::vector<uint32_t>& nbr,
+                       std::vector<uint16_t>& list) {
+    const int mask = (1 << bits) - 1;
+    const int kmap_size = bits == 2 ? 43692 : 4096;
+    std::vector<int> kmap(kmap_size, -1);
+    for (int i = 0; i < G; i++) kmap[kgrid[i]] = i;
+    const int nidx = bits == 2 ? 6561 : 4096;
+    nbr.assign(nidx, 0);
+    std::vector<int64_t> keys(G);
+    for (int idx = 0; idx < nidx; idx++) {
+        int code = 0;
+        if (bits == 2) {
+            int t = idx;
+            for (int j = 0; j < npos; j++) { code |= (t % 3) << (2 * j); t /= 3; }
+        } else {
+            code = idx;
+        }
+        if (kmap[code] >= 0) {
+            nbr[idx] = 0x80000000u | (uint32_t)kmap[code];
+            continue;
+        }
+        for (int i = 0; i < G; i++) {
+            int d2 = 0;
+            for (int j = 0; j < npos; j++) {
+                int p = 2 * ((code >> (bits * j)) & mask) + 1;
+                int q = 2 * ((kgrid[i] >> (bits * j)) & mask) + 1;
+                d2 += (p - q) * (p - q);
+            }
+            keys[i] = (int64_t)d2 * 65536 + i;
+        }
+        std::sort(keys.begin(), keys.end());
+        int ndist = 0, n = 0;
+        int64_t prev = -1;
+        for (int i = 0; i < G; i++) {
+            int64_t d2 = keys[i] / 65536;
+            if (d2 != prev) { ndist++; prev = d2; }
+            if (ndist > nwant) break;
+            n++;
+        }
+        nbr[idx] = ((uint32_t)list.size() << 9) | (uint32_t)n;
+        for (int i = 0; i < n; i++) list.push_back((uint16_t)(keys[i] % 65536));
+    }
+}
+
 cudaError_t iq_tables_create(IqTables** out) {
-    *out = new IqTables{0};
+    struct Spec { const uint16_t* grid; int G, bits, npos, nwant; } specs[5] = {
+        {KGRID_2BIT_256, 256, 2, 8, 2}, {KGRID_2BIT_512, 512, 2, 8, 2}, {KGRID_2BIT_1024, 1024, 2, 8, 1},
+        {KGRID_3BIT_256, 256, 3, 4, 2}, {KGRID_3BIT_512, 512, 3, 4, 3}};
+    std::vector<uint32_t> nbr[5];
+    std::vector<uint16_t> list[5];
+    size_t total = 0;
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    for (int t = 0; t < 5; t++) {
+        build_grid(specs[t].grid, specs[t].G, specs[t].bits, specs[t].npos, specs[t].nwant, nbr[t], list[t]);
+        total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 2 + 16);
+    }
+    char* mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, total);
+    if (e != cudaSuccess) return e;
+    IqTables* T = new IqTables;
+    T->mem = mem;
+    size_t o = 0;
+    for (int t = 0; t < 5; t++) {
+        uint16_t* kg = reinterpret_cast<uint16_t*>(mem + o);
+        o += al(specs[t].G * 2);
+        uint32_t* nb = reinterpret_cast<uint32_t*>(mem + o);
+        o += al(nbr[t].size() * 4);
+        uint16_t* ls = reinterpret_cast<uint16_t*>(mem + o);
+        o += al(list[t].size() * 2 + 16);
+        if ((e = cudaMemcpy(kg, specs[t].grid, specs[t].G * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
+            (e = cudaMemcpy(nb, nbr[t].data(), nbr[t].size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+            (e = cudaMemcpy(ls, list[t].data(), list[t].size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            cudaFree(mem);
+            delete T;
+            return e;
+        }
+        T->g[t] = IqGridDev{kg, nb, ls, specs[t].G};
+    }
+    *out = T;
     return cudaSuccess;
 }
 
-void iq_tables_destroy(IqTables* t) { delete t; }
+void iq_tables_destroy(IqTables* t) {
+    if (t) {
+        cudaFree(t->mem);
+        delete t;
+    }
+}
 
-cudaError_t launch_iq(int, const QuantArgs&, const LaunchCtx&, const IqTables*) { return cudaErrorNotSupported; }
+// ---------------------------------------------------------------------------
+// per-type constants
+// ---------------------------------------------------------------------------
+enum SumKind { SUM_TORCH, SUM_TREE };
+enum Reproj { RP_ALL_PROJ, RP_OFFGRID_NEED, RP_OFFGRID_REDO, RP_ALL_REDO };
+
+template <int T> struct IqT;
+template <> struct IqT<QS_IQ2_XXS> {
+    static constexpr int GS = 32, NSUB = 4, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 13, BB = 66, GID = G_IQ2XXS;
+    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = true;
+    static constexpr int SUMK = SUM_TORCH, RP = RP_ALL_PROJ;
+    static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
+};
+template <> struct IqT<QS_IQ2_XS> {
+    static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 74, GID = G_IQ2XS;
+    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
+    static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
+    static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
+};
+template <> struct IqT<QS_IQ2_S> {
+    static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 82, GID = G_IQ2S;
+    static constexpr bool PARITY = false, ACT_GT0 = false, INIT_QP = false;
+    static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
+    static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 0.9875f;
+};
+template <> struct IqT<QS_IQ3_XXS> {
+    static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 31, BB = 98, GID = G_IQ3XXS;
+    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
+    static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_REDO;
+    static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 1.0125f;
+};
+template <> struct IqT<QS_IQ3_S> {
+    static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 19, BB = 110, GID = G_IQ3S;
+    static constexpr bool PARITY = false, ACT_GT0 = true, INIT_QP = false;
+    static constexpr int SUMK = SUM_TREE, RP = RP_ALL_REDO;
+    static constexpr float EPS = 0.0f, SIGFAC = 2.0f, DMUL = 1.033f;
+};
+
+struct IqParams {
+    float c[32];   // sweep-step numerators
+    float qp[8];   // make_qp numerators (IQ2_XXS initial scale)
+};
+
+constexpr int IQ_WARPS = 4;      // warps per CTA; each warp owns 32 groups
+constexpr int IQ_CAP = 512;      // queued searches per warp
+constexpr int IQ_FINAL = 15;     // tag slot of the final reprojection
+
+template <class Tr>
+struct IqWarpSmem {
+    static constexpr int NB = IQ_CAP / (32 * Tr::NSUB);  // sweep steps per batch
+    float xv[32][Tr::GS];        // search-space values of every group (|x|, parity-folded)
+    float wv[32][Tr::GS];        // sqrt of the weights
+    float tbl[32][32];           // per-lane distance terms [position * NLEV + level][lane]
+    unsigned long long key[IQ_CAP];  // best (d2 bits << 32 | position) per search; sigma2 squares alias it
+    uint32_t off[IQ_CAP];
+    uint32_t start[IQ_CAP + 1];
+    uint16_t len[IQ_CAP];
+    uint16_t tag[IQ_CAP];        // group | slot << 5 | subgroup << 9
+    uint16_t win[32][NB][Tr::NSUB];  // resolved grid index (| 0x8000 when it came from a search)
+    float gr[32];                // per-group reciprocal of the step denominator
+    float gsc[32];               // per-group final scale (reprojection)
+    float part[4][8];
+    int nq;
+};
+
+template <class Tr>
+constexpr size_t iq_smem_bytes() {
+    return IQ_WARPS * sizeof(IqWarpSmem<Tr>) + 1024 * 2 + 64 * 4 + 16 * Tr::BB + 64;
+}
+
+__device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    total = __shfl_sync(0xffffffffu, x, 31);
+    return x - v;
+}
+
+// Solve every queued search of this warp. Slot s of group g uses the scale 1/(gr[g]*c[s0+s])
+// (the sweep) or gsc[g] (the final reprojection).
+template <class Tr>
+__device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, const uint16_t* s_kgrid, const float* s_c, int s0,
+                         int lane) {
+    const int P = W.nq;
+    if (P == 0) return;
+    // exclusive scan of the list lengths
+    const int per = (P + 31) / 32;
+    const int i0 = min(P, lane * per), i1 = min(P, i0 + per);
+    int loc = 0;
+    for (int i = i0; i < i1; i++) loc += W.len[i];
+    int T;
+    int run = warp_excl_scan(loc, lane, T);
+    for (int i = i0; i < i1; i++) { W.start[i] = run; run += W.len[i]; }
+    if (lane == 0) W.start[P] = T;
+    for (int i = lane; i < P; i += 32) W.key[i] = ~0ull;
+    __syncwarp();
+
+    // this lane's slice of the concatenated candidate stream
+    const uint32_t t0 = (uint32_t)(((uint64_t)T * lane) / 32), t1 = (uint32_t)(((uint64_t)T * (lane + 1)) / 32);
+    if (t0 < t1) {
+        int lo = 0, hi = P - 1;  // last search whose start <= t0
+        while (lo < hi) {
+            int mid = (lo + hi + 1) >> 1;
+            if (W.start[mid] <= t0) lo = mid; else hi = mid - 1;
+        }
+        int p = lo;
+        uint32_t t = t0;
+        while (t < t1 && p < P) {
+            const uint32_t st = W.start[p], n = W.len[p], off = W.off[p];
+            const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
+            const float sc = slot == IQ_FINAL ? W.gsc[g] : rcp_rn(W.gr[g] * s_c[s0 + slot]);
+            // distance terms (wv * (sc * v - xv)) * (sc * v - xv) for v = 2l + 1
+#pragma unroll
+            for (int j = 0; j < Tr::NPOS; j++) {
+                const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
+#pragma unroll
+                for (int l = 0; l < Tr::NLEV; l++) {
+                    const float df = sc * (float)(2 * l + 1) - xj;
+                    W.tbl[j * Tr::NLEV + l][lane] = (wj * df) * df;
+                }
+            }
+            const uint32_t pe = min(n, t1 - st);
+            unsigned long long best = ~0ull;
+#pragma unroll 4
+            for (uint32_t pos = t - st; pos < pe; pos++) {
+                const int code = s_kgrid[__ldg(G.list + off + pos)];
+                float d2 = W.tbl[(code & (Tr::NLEV - 1))][lane];
+#pragma unroll
+                for (int j = 1; j < Tr::NPOS; j++)
+                    d2 = __fadd_rn(d2, W.tbl[j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))][lane]);
+                const unsigned long long k = ((unsigned long long)__float_as_uint(d2) << 32) | pos;
+                best = k < best ? k : best;
+            }
+            atomicMin(&W.key[p], best);
+            t = st + pe;
+            p++;
+        }
+    }
+    __syncwarp();
+    for (int i = lane; i < P; i += 32) {
+        const int tg = W.tag[i], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
+        const uint32_t pos = (uint32_t)W.key[i];
+        W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)(__ldg(G.list + W.off[i] + pos) | 0x8000);
+    }
+    __syncwarp();
+    if (lane == 0) W.nq = 0;
+    __syncwarp();
+}
+
+// Tentative code of subgroup q at inverse scale inv; on-grid codes resolve at once
+// (writes win), off-grid ones are queued. Returns 1 if queued.
+template <class Tr>
+__device__ __forceinline__ int iq_code(const float* xval, int q, float inv, const IqGridDev& G, uint32_t& v) {
+    int idx = 0, mul = 1;
+#pragma unroll
+    for (int j = 0; j < Tr::NPOS; j++) {
+        const int l = (int)clampf(rintf(0.5f * (inv * xval[q * Tr::NPOS + j] - 1.0f)), 0.0f, (float)Tr::MAXL);
+        if (Tr::BITS == 2) { idx += l * mul; mul *= 3; }
+        else idx |= l << (3 * j);
+    }
+    v = __ldg(G.nbr + idx);
+    return (v >> 31) ? 0 : 1;
+}
+
+template <class Tr>
+__device__ __forceinline__ void iq_enqueue(IqWarpSmem<Tr>& W, int lane, int nmine, const uint32_t* vs, const int* qs,
+                                           int slot) {
+    int tot;
+    const int base = W.nq + warp_excl_scan(nmine, lane, tot);
+    for (int i = 0; i < nmine; i++) {
+        W.off[base + i] = vs[i] >> 9;
+        W.len[base + i] = (uint16_t)(vs[i] & 511);
+        W.tag[base + i] = (uint16_t)(lane | (slot << 5) | (qs[i] << 9));
+    }
+    __syncwarp();
+    if (lane == 0) W.nq += tot;
+    __syncwarp();
+}
+
+// grid values (2l+1) of the winners of one group -> q[GS]
+template <class Tr>
+__device__ __forceinline__ void iq_decode(const uint16_t* s_kgrid, const uint16_t* win, float* q) {
+#pragma unroll
+    for (int s = 0; s < Tr::NSUB; s++) {
+        const int code = s_kgrid[win[s] & 0x7FFF];
+#pragma unroll
+        for (int j = 0; j < Tr::NPOS; j++) q[s * Tr::NPOS + j] = (float)(2 * ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1)) + 1);
+    }
+}
+
+template <class Tr>
+__device__ __forceinline__ void iq_sums(const float* w, const float* xval, const float* q, float& sumqx, float& sumq2) {
+    float a[Tr::GS], b[Tr::GS];
+#pragma unroll
+    for (int i = 0; i < Tr::GS; i++) {
+        a[i] = (w[i] * xval[i]) * q[i];
+        b[i] = (w[i] * q[i]) * q[i];
+    }
+    if (Tr::SUMK == SUM_TORCH) {
+        sumqx = torch_sum<Tr::GS>(a);
+        sumq2 = torch_sum<Tr::GS>(b);
+    } else {
+        sumqx = tree_sum<Tr::GS>(a);
+        sumq2 = tree_sum<Tr::GS>(b);
+    }
+}
+
+template <int TYPE, bool IMAT>
+__global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDev G, IqParams prm) {
+    using Tr = IqT<TYPE>;
+    using WS = IqWarpSmem<Tr>;
+    constexpr int GS = Tr::GS, NSUB = Tr::NSUB, SBG = QK_K / GS, SBW = 32 / SBG, SBT = IQ_WARPS * SBW, BB = Tr::BB;
+    constexpr int NB = WS::NB;
+    extern __shared__ __align__(16) unsigned char smem[];
+    WS* wsm = reinterpret_cast<WS*>(smem);
+    uint16_t* s_kgrid = reinterpret_cast<uint16_t*>(smem + IQ_WARPS * sizeof(WS));
+    float* s_c = reinterpret_cast<float*>(s_kgrid + 1024);
+    float* s_qp = s_c + 32;
+    uint8_t* s_out = reinterpret_cast<uint8_t*>(s_qp + 32);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    WS& W = wsm[warp];
+    for (int i = tid; i < G.grid; i += blockDim.x) s_kgrid[i] = G.kgrid[i];
+    if (tid < 32) s_c[tid] = prm.c[tid];
+    if (tid < 8) s_qp[tid] = prm.qp[tid];
+    if (lane == 0) W.nq = 0;
+    __syncthreads();
+
+    const int sbl = lane / SBG, gl = lane % SBG;  // superblock within the warp, group within it
+    for (int64_t tile = blockIdx.x; tile * SBT < a.nblk; tile += gridDim.x) {
+        const int64_t b = min(tile * SBT + warp * SBW + sbl, a.nblk - 1);
+        float x[GS], w[GS], xval[GS];
+        load_row<GS>(a.src, b * QK_K + gl * GS, a.src_type, x);
+
+        // weights (iq2.py:429-431, iq2_xs.py:27-29, iq2_s.py:28-30, iq3_xxs.py:40-45)
+        if (IMAT) {
+            float* sq = reinterpret_cast<float*>(W.key) + sbl * QK_K;
+#pragma unroll
+            for (int i = 0; i < GS; i++) sq[gl * GS + i] = x[i] * x[i];
+            __syncwarp();
+            if (gl < 8) W.part[sbl][gl] = sb_sum256_partial(sq, gl);
+            __syncwarp();
+            const float sigma2 = __fdiv_rn(Tr::SIGFAC * sb_sum256_finish(W.part[sbl]), 256.0f);
+            float qv[GS];
+            load_f32<GS>(a.qw + (b % a.nblk_row) * QK_K + gl * GS, qv);
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = qv[i] * sqrtf(sigma2 + x[i] * x[i]);
+            __syncwarp();
+        } else {
+#pragma unroll
+            for (int i = 0; i < GS; i++) w[i] = x[i] * x[i];
+        }
+
+        // signs: parity fold (iq2.py:439-449) or explicit bits (iq2_s.py:32-34, iq3_s.py:51-55)
+        uint32_t signs = 0;  // 7 or 8 bits per 8 values
+#pragma unroll
+        for (int s = 0; s < GS / 8; s++) {
+            int sb = 0, nneg = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                xval[8 * s + j] = fabsf(x[8 * s + j]);
+                if (x[8 * s + j] < 0.0f) { sb |= 1 << j; nneg++; }
+            }
+            if (Tr::PARITY) {
+                if (nneg & 1) {
+                    int imin = 0;
+                    float m = (w[8 * s] * x[8 * s]) * x[8 * s];
+#pragma unroll
+                    for (int j = 1; j < 8; j++) {
+                        const float v = (w[8 * s + j] * x[8 * s + j]) * x[8 * s + j];
+                        if (v < m) { m = v; imin = j; }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        if (j == imin) xval[8 * s + j] = -xval[8 * s + j];
+                    sb ^= 1 << imin;
+                }
+                signs |= (uint32_t)(sb & 127) << (7 * s);
+            } else {
+                signs |= (uint32_t)sb << (8 * s);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < GS; i++) {
+            W.xv[lane][i] = xval[i];
+            W.wv[lane][i] = sqrtf(w[i]);
+        }
+
+        const float gmax = max_of<GS>(xval);
+        bool active = Tr::ACT_GT0 ? gmax > 0.0f : gmax >= Tr::EPS;
+        float scale, r;
+        if (Tr::INIT_QP) {  // iq2.py:458-463
+            float Lq[GS];
+            const float scale0 = qp_search<GS>(xval, w, 4.0f, s_qp, Lq);
+            const float eff = scale0 * 3.0f;
+            active = active && eff > 0.0f;
+            r = rcp_rn(active ? eff : 1.0f);
+            scale = scale0;
+        } else {
+            r = rcp_rn(active ? gmax : 1.0f);
+            if (TYPE == QS_IQ2_XS || TYPE == QS_IQ2_S) scale = active ? __fdiv_rn(gmax, 5.0f) : 0.0f;
+            else scale = __fdiv_rn(gmax, 15.0f);
+        }
+        W.gr[lane] = r;
+        float best = 0.0f;
+        uint16_t cur[NSUB];
+#pragma unroll
+        for (int s = 0; s < NSUB; s++) cur[s] = Tr::RP == RP_ALL_REDO ? 0x8000 : 0;  // og_init: IQ3_S starts off-grid
+        __syncwarp();
+
+        // sweep over the candidate scales, NB steps per batch of searches
+        for (int s0 = 0; s0 < Tr::NSTEP; s0 += NB) {
+            const int nb = min(NB, Tr::NSTEP - s0);
+            for (int j = 0; j < nb; j++) {
+                const float inv = r * s_c[s0 + j];
+                uint32_t vs[NSUB];
+                int qs[NSUB], nm = 0;
+#pragma unroll
+                for (int q = 0; q < NSUB; q++) {
+                    uint32_t v;
+                    if (iq_code<Tr>(xval, q, inv, G, v)) { vs[nm] = v; qs[nm] = q; nm++; }
+                    else W.win[lane][j][q] = (uint16_t)(v & 0x7FFF);
+                }
+                iq_enqueue<Tr>(W, lane, nm, vs, qs, j);
+            }
+            iq_flush<Tr>(W, G, s_kgrid, s_c, s0, lane);
+            for (int j = 0; j < nb; j++) {
+                float qv[GS], sumqx, sumq2;
+                iq_decode<Tr>(s_kgrid, W.win[lane][j], qv);
+                iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
+                if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
+                    const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
+                    scale = ns;
+                    best = ns * sumqx;
+#pragma unroll
+                    for (int q = 0; q < NSUB; q++) cur[q] = W.win[lane][j][q];
+                }
+            }
+            __syncwarp();
+        }
+
+        // final reprojection at the accepted scale + least-squares refit
+        bool anyoff = false, allon = true;
+#pragma unroll
+        for (int q = 0; q < NSUB; q++) { anyoff |= (cur[q] & 0x8000) != 0; allon &= (cur[q] & 0x8000) == 0; }
+        bool redo;
+        float inv;
+        if (Tr::RP == RP_ALL_PROJ) {
+            redo = active && scale > 0.0f;
+            inv = rcp_rn(redo ? scale : 1.0f);
+        } else if (Tr::RP == RP_OFFGRID_NEED) {
+            redo = active && scale > 0.0f && !allon;
+            inv = rcp_rn(scale > 0.0f ? scale : 1.0f);
+        } else {
+            redo = active && anyoff && scale > 0.0f;
+            inv = rcp_rn(redo ? scale : 1.0f);
+        }
+        W.gsc[lane] = scale;
+        {
+            uint32_t vs[NSUB];
+            int qs[NSUB], nm = 0;
+#pragma unroll
+            for (int q = 0; q < NSUB; q++) {
+                const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & 0x8000));
+                W.win[lane][0][q] = cur[q];
+                if (want) {
+                    uint32_t v;
+                    if (iq_code<Tr>(xval, q, inv, G, v)) { vs[nm] = v; qs[nm] = q; nm++; }
+                    else W.win[lane][0][q] = (uint16_t)(v & 0x7FFF);
+                }
+            }
+            __syncwarp();
+            iq_enqueue<Tr>(W, lane, nm, vs, qs, IQ_FINAL);
+        }
+        iq_flush<Tr>(W, G, s_kgrid, s_c, 0, lane);
+        uint16_t fin[NSUB];
+#pragma unroll
+        for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][0][q] & 0x7FFF;
+        {
+            float qv[GS], sumqx, sumq2;
+            iq_decode<Tr>(s_kgrid, fin, qv);
+            iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
+            if (redo && sumq2 > 0.0f) scale = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
+        }
+        if (!redo) {
+#pragma unroll
+            for (int q = 0; q < NSUB; q++) fin[q] = cur[q] & 0x7FFF;
+        }
+        // negative least-squares scale: flip the scale and all the signs
+        if (active && scale < 0.0f) {
+            scale = -scale;
+            signs = ~signs & (Tr::PARITY ? (GS == 32 ? 0x0FFFFFFFu : 0x3FFFu) : (GS == 32 ? 0xFFFFFFFFu : 0xFFFFu));
+        }
+        const float sc_g = active ? scale : 0.0f;
+
+        // superblock: d = max_scale / 31, 4-bit sub-scales (iq2.py:87-108, iq2xs_common.py:345-355)
+        float max_scale = sc_g;
+#pragma unroll
+        for (int o = 1; o < SBG; o <<= 1) {
+            const float t = __shfl_xor_sync(0xffffffffu, max_scale, o);
+            max_scale = t > max_scale ? t : max_scale;
+        }
+        const bool has = max_scale > 0.0f;
+        const float d = __fdiv_rn(max_scale, 31.0f);
+        const float inv_d = rcp_rn(has ? d : 1.0f);
+        const int lnib = has ? (int)clampf(rintf(0.5f * (inv_d * sc_g - 1.0f)), 0.0f, 15.0f) : 0;
+        uint8_t* o = s_out + (warp * SBW + sbl) * BB;
+        if (gl == 0) {
+            const uint16_t dh = f16_bits(has ? (Tr::DMUL == 1.0f ? d : d * Tr::DMUL) : 0.0f);
+            o[0] = (uint8_t)dh;
+            o[1] = (uint8_t)(dh >> 8);
+        }
+        if (TYPE == QS_IQ2_XXS) {
+            uint32_t lo = 0, hi = 0;
+            if (active && has) {
+#pragma unroll
+                for (int q = 0; q < 4; q++) lo |= (uint32_t)fin[q] << (8 * q);
+                hi = signs;
+            }
+            if (has) hi |= (uint32_t)lnib << 28;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                o[2 + 8 * gl + i] = (uint8_t)(lo >> (8 * i));
+                o[6 + 8 * gl + i] = (uint8_t)(hi >> (8 * i));
+            }
+        } else if (TYPE == QS_IQ2_XS) {
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const uint32_t v = (active && has) ? ((uint32_t)fin[q] | (((signs >> (7 * q)) & 127) << 9)) : 0;
+                o[2 + 4 * gl + 2 * q] = (uint8_t)v;
+                o[3 + 4 * gl + 2 * q] = (uint8_t)(v >> 8);
+            }
+            const int ln1 = __shfl_down_sync(0xffffffffu, lnib, 1);
+            if ((gl & 1) == 0) o[66 + gl / 2] = (uint8_t)(lnib | (ln1 << 4));
+        } else if (TYPE == QS_IQ2_S) {
+            int qh = 0;
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const int gi = active ? fin[q] : 0;
+                o[2 + 2 * gl + q] = (uint8_t)(gi & 255);
+                o[34 + 2 * gl + q] = (uint8_t)(active ? (signs >> (8 * q)) & 255 : 0);
+                qh |= (gi >> 8) << (2 * (2 * (gl & 1) + q));
+            }
+            const int qh1 = __shfl_down_sync(0xffffffffu, qh, 1);
+            const int ln1 = __shfl_down_sync(0xffffffffu, lnib, 1);
+            if ((gl & 1) == 0) {
+                o[66 + gl / 2] = (uint8_t)(qh | qh1);
+                o[74 + gl / 2] = (uint8_t)(lnib | (ln1 << 4));
+            }
+        } else if (TYPE == QS_IQ3_XXS) {
+#pragma unroll
+            for (int q = 0; q < 8; q++) o[2 + 8 * gl + q] = (uint8_t)((active && has) ? fin[q] : 0);
+            const uint32_t word = has ? ((active ? signs : 0) | ((uint32_t)lnib << 28)) : 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) o[66 + 4 * gl + i] = (uint8_t)(word >> (8 * i));
+        } else {  // IQ3_S: live groups compact toward the front of qs / signs (iq3_s.py:113-122)
+#pragma unroll
+            for (int i = 0; i < 8; i++) o[2 + 8 * gl + i] = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) o[74 + 4 * gl + i] = 0;
+            const unsigned act = __ballot_sync(0xffffffffu, active);
+            const unsigned mine = (act >> (sbl * SBG)) & ((1u << SBG) - 1);
+            const int slot = __popc(mine & ((1u << gl) - 1));
+            __syncwarp();
+            int qh = 0;
+            if (active) {
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    o[2 + 8 * slot + q] = (uint8_t)(fin[q] & 255);
+                    qh |= (fin[q] >> 8) << q;
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) o[74 + 4 * slot + i] = (uint8_t)(signs >> (8 * i));
+            }
+            o[66 + gl] = (uint8_t)qh;
+            const int ln1 = __shfl_down_sync(0xffffffffu, lnib, 1);
+            if ((gl & 1) == 0) o[106 + gl / 2] = (uint8_t)(lnib | (ln1 << 4));
+        }
+        __syncthreads();
+        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, blockDim.x);
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host launch
+// ---------------------------------------------------------------------------
+template <int TYPE, bool IMAT>
+static cudaError_t launch_one(const QuantArgs& a, const LaunchCtx& ctx, const IqTables* t, const IqParams& p) {
+    using Tr = IqT<TYPE>;
+    constexpr size_t smem = iq_smem_bytes<Tr>();
+    auto k = iq_kernel<TYPE, IMAT>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, IQ_WARPS * 32, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    constexpr int SBT = IQ_WARPS * (32 / (QK_K / Tr::GS));
+    const int64_t tiles = (a.nblk + SBT - 1) / SBT;
+    const int64_t g = (int64_t)per_sm * ctx.num_sms;
+    const int grid = (int)(tiles < g ? tiles : g);
+    k<<<grid, IQ_WARPS * 32, smem, ctx.stream>>>(a, t->g[Tr::GID], p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_iq(int type, const QuantArgs& a, const LaunchCtx& ctx, const IqTables* t) {
+    IqParams p;
+    memset(&p, 0, sizeof(p));
+    const bool imat = a.qw != nullptr;
+    switch (type) {
+    case QS_IQ2_XXS: {
+        for (int s = -6; s <= 6; s++) p.c[s + 6] = (float)(5.0 + 0.1 * s);  // iq2.py:470 (double, then f32)
+        int j = 0;
+        for (int s = -4; s <= 4; s++) if (s) p.qp[j++] = (float)(0.1 * s + 4.0);  // iq2.py:387
+        return imat ? launch_one<QS_IQ2_XXS, true>(a, ctx, t, p) : cudaErrorInvalidValue;
+    }
+    case QS_IQ2_XS:
+    case QS_IQ2_S:
+        for (int s = -9; s <= 9; s++) p.c[s + 9] = 5.0f + (float)s * 0.1f;  // iq2xs_common.py:21
+        if (!imat) return cudaErrorInvalidValue;
+        return type == QS_IQ2_XS ? launch_one<QS_IQ2_XS, true>(a, ctx, t, p) : launch_one<QS_IQ2_S, true>(a, ctx, t, p);
+    case QS_IQ3_XXS:
+        for (int s = -15; s <= 15; s++) p.c[s + 15] = 15.0f + (float)s * 0.2f;  // iq3_xxs.py:22
+        return imat ? launch_one<QS_IQ3_XXS, true>(a, ctx, t, p) : launch_one<QS_IQ3_XXS, false>(a, ctx, t, p);
+    case QS_IQ3_S:
+        for (int s = -9; s <= 9; s++) p.c[s + 9] = 15.0f + (float)s * 0.2f;  // iq3_s.py:22
+        return imat ? launch_one<QS_IQ3_S, true>(a, ctx, t, p) : launch_one<QS_IQ3_S, false>(a, ctx, t, p);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
 
 }  // namespace qs

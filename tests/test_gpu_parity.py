@@ -15,7 +15,8 @@ from kernels import _native
 pytestmark = pytest.mark.gpu
 
 GT = oracle.TYPE_IDS
-GPU_TYPES = ["q4_0", "q2_k", "q3_k", "q4_k", "q5_k", "q6_k", "iq4_xs"]
+GPU_TYPES = ["q4_0", "q2_k", "q3_k", "q4_k", "q5_k", "q6_k", "iq4_xs",
+             "iq2_xxs", "iq2_xs", "iq2_s", "iq3_xxs", "iq3_s"]
 
 
 def dev_input(inputs, src):
