@@ -32,7 +32,7 @@ namespace qs {
 struct IqGridDev {
     const uint16_t* kgrid;  // grid index -> code
     const uint32_t* nbr;    // code index -> 0x80000000 | grid index (on grid) or off << 9 | len
-    const uint16_t* list;   // neighbour lists (grid indices), (distance, index) order
+    const uint32_t* list;   // neighbour lists, code << 16 | grid index, (distance, index) order
     int grid;
 };
 
@@ -47,7 +47,7 @@ enum { G_IQ2XXS = 0, G_IQ2XS, G_IQ2S, G_IQ3XXS, G_IQ3S };
 // iq2.py:31-74, iq2xs_common.py:41-95, iq3_common.py:29-68). IQ2 codes are indexed in
 // base 3 because sweep levels are clamped to 0..2, IQ3 codes directly (levels 0..7).
 static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwant, std::vector<uint32_t>& nbr,
-                       std::vector<uint16_t>& list) {
+                       std::vector<uint32_t>& list) {
     const int mask = (1 << bits) - 1;
     const int kmap_size = bits == 2 ? 43692 : 4096;
     std::vector<int> kmap(kmap_size, -1);
@@ -86,7 +86,10 @@ static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwa
             n++;
         }
         nbr[idx] = ((uint32_t)list.size() << 9) | (uint32_t)n;
-        for (int i = 0; i < n; i++) list.push_back((uint16_t)(keys[i] % 65536));
+        for (int i = 0; i < n; i++) {
+            const int gi = (int)(keys[i] % 65536);
+            list.push_back(((uint32_t)kgrid[gi] << 16) | (uint32_t)gi);
+        }
     }
 }
 
@@ -95,12 +98,12 @@ cudaError_t iq_tables_create(IqTables** out) {
         {KGRID_2BIT_256, 256, 2, 8, 2}, {KGRID_2BIT_512, 512, 2, 8, 2}, {KGRID_2BIT_1024, 1024, 2, 8, 1},
         {KGRID_3BIT_256, 256, 3, 4, 2}, {KGRID_3BIT_512, 512, 3, 4, 3}};
     std::vector<uint32_t> nbr[5];
-    std::vector<uint16_t> list[5];
+    std::vector<uint32_t> list[5];
     size_t total = 0;
     auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
     for (int t = 0; t < 5; t++) {
         build_grid(specs[t].grid, specs[t].G, specs[t].bits, specs[t].npos, specs[t].nwant, nbr[t], list[t]);
-        total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 2 + 16);
+        total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 4 + 16);
     }
     char* mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, total);
@@ -113,11 +116,11 @@ cudaError_t iq_tables_create(IqTables** out) {
         o += al(specs[t].G * 2);
         uint32_t* nb = reinterpret_cast<uint32_t*>(mem + o);
         o += al(nbr[t].size() * 4);
-        uint16_t* ls = reinterpret_cast<uint16_t*>(mem + o);
-        o += al(list[t].size() * 2 + 16);
+        uint32_t* ls = reinterpret_cast<uint32_t*>(mem + o);
+        o += al(list[t].size() * 4 + 16);
         if ((e = cudaMemcpy(kg, specs[t].grid, specs[t].G * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
             (e = cudaMemcpy(nb, nbr[t].data(), nbr[t].size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
-            (e = cudaMemcpy(ls, list[t].data(), list[t].size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            (e = cudaMemcpy(ls, list[t].data(), list[t].size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) {
             cudaFree(mem);
             delete T;
             return e;
@@ -143,30 +146,35 @@ enum Reproj { RP_ALL_PROJ, RP_OFFGRID_NEED, RP_OFFGRID_REDO, RP_ALL_REDO };
 
 template <int T> struct IqT;
 template <> struct IqT<QS_IQ2_XXS> {
+    static constexpr int LPP = 32;  // lanes per neighbour search
     static constexpr int GS = 32, NSUB = 4, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 13, BB = 66, GID = G_IQ2XXS;
     static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = true;
     static constexpr int SUMK = SUM_TORCH, RP = RP_ALL_PROJ;
     static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
 };
 template <> struct IqT<QS_IQ2_XS> {
+    static constexpr int LPP = 32;  // lanes per neighbour search
     static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 74, GID = G_IQ2XS;
     static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
     static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
 };
 template <> struct IqT<QS_IQ2_S> {
+    static constexpr int LPP = 16;  // lanes per neighbour search
     static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 82, GID = G_IQ2S;
     static constexpr bool PARITY = false, ACT_GT0 = false, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
     static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 0.9875f;
 };
 template <> struct IqT<QS_IQ3_XXS> {
+    static constexpr int LPP = 8;  // lanes per neighbour search
     static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 31, BB = 98, GID = G_IQ3XXS;
     static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_REDO;
     static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 1.0125f;
 };
 template <> struct IqT<QS_IQ3_S> {
+    static constexpr int LPP = 16;  // lanes per neighbour search
     static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 19, BB = 110, GID = G_IQ3S;
     static constexpr bool PARITY = false, ACT_GT0 = true, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_ALL_REDO;
@@ -185,17 +193,18 @@ constexpr int IQ_FINAL = 15;     // tag slot of the final reprojection
 template <class Tr>
 struct IqWarpSmem {
     static constexpr int NB = IQ_CAP / (32 * Tr::NSUB);  // sweep steps per batch
+    static constexpr int NS = 32 / Tr::LPP;              // searches in flight per warp
+    static constexpr int RED = 2 * 32 * (Tr::LPP + 1);
     float xv[32][Tr::GS];        // search-space values of every group (|x|, parity-folded)
     float wv[32][Tr::GS];        // sqrt of the weights
-    float tbl[32][32];           // per-lane distance terms [position * NLEV + level][lane]
-    unsigned long long key[IQ_CAP];  // best (d2 bits << 32 | position) per search; sigma2 squares alias it
+    // sigma2 squares during the weights, then per-lane search minima [search][lane] (d2, position)
+    float scratch[RED > 1024 ? RED : 1024];
+    float tbl[32 * NS];          // distance terms of the searches in flight [position * NLEV + level][search]
+    float psc[32][NB + 1];       // per group: search scale of each batch step, then the final scale
     uint32_t off[IQ_CAP];
-    uint32_t start[IQ_CAP + 1];
     uint16_t len[IQ_CAP];
     uint16_t tag[IQ_CAP];        // group | slot << 5 | subgroup << 9
     uint16_t win[32][NB][Tr::NSUB];  // resolved grid index (| 0x8000 when it came from a search)
-    float gr[32];                // per-group reciprocal of the step denominator
-    float gsc[32];               // per-group final scale (reprojection)
     float part[4][8];
     int nq;
 };
@@ -216,73 +225,70 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
     return x - v;
 }
 
-// Solve every queued search of this warp. Slot s of group g uses the scale 1/(gr[g]*c[s0+s])
-// (the sweep) or gsc[g] (the final reprojection).
+// Solve every queued search of this warp: LPP lanes per search, 32/LPP searches at a
+// time. The LPP lanes first tabulate the search's distance terms (one table entry per
+// lane), then take candidates c = lane, lane + LPP, ... in list order keeping their first
+// minimum; the per-lane minima of 32 searches are transposed through shared memory and
+// lane i merges search i (smaller d2, then smaller position: the reference's argmin).
 template <class Tr>
-__device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, const uint16_t* s_kgrid, const float* s_c, int s0,
-                         int lane) {
+__device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
+    using WS = IqWarpSmem<Tr>;
+    constexpr int LPP = Tr::LPP, NS = WS::NS, NE = Tr::NPOS * Tr::NLEV, RS = LPP + 1;
+    static_assert(NE == 32, "term table holds 32 entries");
     const int P = W.nq;
-    if (P == 0) return;
-    // exclusive scan of the list lengths
-    const int per = (P + 31) / 32;
-    const int i0 = min(P, lane * per), i1 = min(P, i0 + per);
-    int loc = 0;
-    for (int i = i0; i < i1; i++) loc += W.len[i];
-    int T;
-    int run = warp_excl_scan(loc, lane, T);
-    for (int i = i0; i < i1; i++) { W.start[i] = run; run += W.len[i]; }
-    if (lane == 0) W.start[P] = T;
-    for (int i = lane; i < P; i += 32) W.key[i] = ~0ull;
-    __syncwarp();
-
-    // this lane's slice of the concatenated candidate stream
-    const uint32_t t0 = (uint32_t)(((uint64_t)T * lane) / 32), t1 = (uint32_t)(((uint64_t)T * (lane + 1)) / 32);
-    if (t0 < t1) {
-        int lo = 0, hi = P - 1;  // last search whose start <= t0
-        while (lo < hi) {
-            int mid = (lo + hi + 1) >> 1;
-            if (W.start[mid] <= t0) lo = mid; else hi = mid - 1;
-        }
-        int p = lo;
-        uint32_t t = t0;
-        while (t < t1 && p < P) {
-            const uint32_t st = W.start[p], n = W.len[p], off = W.off[p];
-            const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
-            const float sc = slot == IQ_FINAL ? W.gsc[g] : rcp_rn(W.gr[g] * s_c[s0 + slot]);
-            // distance terms (wv * (sc * v - xv)) * (sc * v - xv) for v = 2l + 1
+    const int sub = lane / LPP, sl = lane % LPP;
+    float* red_d = W.scratch;
+    int* red_p = reinterpret_cast<int*>(W.scratch) + 32 * RS;
+    for (int pb = 0; pb < P; pb += 32) {
+        const int nbp = min(32, P - pb);
+        for (int k = 0; k < nbp; k += NS) {
+            const int p = pb + k + sub;
+            int len = 0;
+            uint32_t off = 0;
+            if (k + sub < nbp) {
+                off = W.off[p];
+                len = W.len[p];
+                const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
+                const float sc = W.psc[g][slot == IQ_FINAL ? WS::NB : slot];
 #pragma unroll
-            for (int j = 0; j < Tr::NPOS; j++) {
-                const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
-#pragma unroll
-                for (int l = 0; l < Tr::NLEV; l++) {
+                for (int e = sl; e < NE; e += LPP) {
+                    const int j = e / Tr::NLEV, l = e % Tr::NLEV;
+                    const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
                     const float df = sc * (float)(2 * l + 1) - xj;
-                    W.tbl[j * Tr::NLEV + l][lane] = (wj * df) * df;
+                    W.tbl[e * NS + sub] = (wj * df) * df;
                 }
             }
-            const uint32_t pe = min(n, t1 - st);
-            unsigned long long best = ~0ull;
-#pragma unroll 4
-            for (uint32_t pos = t - st; pos < pe; pos++) {
-                const int code = s_kgrid[__ldg(G.list + off + pos)];
-                float d2 = W.tbl[(code & (Tr::NLEV - 1))][lane];
+            __syncwarp();
+            float bd = __int_as_float(0x7f800000);
+            int bp = 0x7fffffff;
+#pragma unroll 2
+            for (int c = sl; c < len; c += LPP) {
+                const int code = (int)(__ldg(G.list + off + c) >> 16);
+                float d2 = W.tbl[(code & (Tr::NLEV - 1)) * NS + sub];
 #pragma unroll
                 for (int j = 1; j < Tr::NPOS; j++)
-                    d2 = __fadd_rn(d2, W.tbl[j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))][lane]);
-                const unsigned long long k = ((unsigned long long)__float_as_uint(d2) << 32) | pos;
-                best = k < best ? k : best;
+                    d2 = __fadd_rn(d2, W.tbl[(j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))) * NS + sub]);
+                if (d2 < bd || bp == 0x7fffffff) { bd = d2; bp = c; }
             }
-            atomicMin(&W.key[p], best);
-            t = st + pe;
-            p++;
+            red_d[(k + sub) * RS + sl] = bd;
+            red_p[(k + sub) * RS + sl] = bp;
+            __syncwarp();
         }
+        if (lane < nbp) {
+            float bd = red_d[lane * RS];
+            int bp = red_p[lane * RS];
+#pragma unroll 4
+            for (int c = 1; c < LPP; c++) {
+                const float d = red_d[lane * RS + c];
+                const int pp = red_p[lane * RS + c];
+                if (d < bd || (d == bd && pp < bp)) { bd = d; bp = pp; }
+            }
+            const int p = pb + lane;
+            const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
+            W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)((__ldg(G.list + W.off[p] + bp) & 0xFFFF) | 0x8000);
+        }
+        __syncwarp();
     }
-    __syncwarp();
-    for (int i = lane; i < P; i += 32) {
-        const int tg = W.tag[i], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
-        const uint32_t pos = (uint32_t)W.key[i];
-        W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)(__ldg(G.list + W.off[i] + pos) | 0x8000);
-    }
-    __syncwarp();
     if (lane == 0) W.nq = 0;
     __syncwarp();
 }
@@ -374,7 +380,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
 
         // weights (iq2.py:429-431, iq2_xs.py:27-29, iq2_s.py:28-30, iq3_xxs.py:40-45)
         if (IMAT) {
-            float* sq = reinterpret_cast<float*>(W.key) + sbl * QK_K;
+            float* sq = W.scratch + sbl * QK_K;
 #pragma unroll
             for (int i = 0; i < GS; i++) sq[gl * GS + i] = x[i] * x[i];
             __syncwarp();
@@ -441,7 +447,6 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             if (TYPE == QS_IQ2_XS || TYPE == QS_IQ2_S) scale = active ? __fdiv_rn(gmax, 5.0f) : 0.0f;
             else scale = __fdiv_rn(gmax, 15.0f);
         }
-        W.gr[lane] = r;
         float best = 0.0f;
         uint16_t cur[NSUB];
 #pragma unroll
@@ -453,6 +458,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             const int nb = min(NB, Tr::NSTEP - s0);
             for (int j = 0; j < nb; j++) {
                 const float inv = r * s_c[s0 + j];
+                W.psc[lane][j] = rcp_rn(inv);
                 uint32_t vs[NSUB];
                 int qs[NSUB], nm = 0;
 #pragma unroll
@@ -463,7 +469,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
                 }
                 iq_enqueue<Tr>(W, lane, nm, vs, qs, j);
             }
-            iq_flush<Tr>(W, G, s_kgrid, s_c, s0, lane);
+            iq_flush<Tr>(W, G, lane);
             for (int j = 0; j < nb; j++) {
                 float qv[GS], sumqx, sumq2;
                 iq_decode<Tr>(s_kgrid, W.win[lane][j], qv);
@@ -495,7 +501,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             redo = active && anyoff && scale > 0.0f;
             inv = rcp_rn(redo ? scale : 1.0f);
         }
-        W.gsc[lane] = scale;
+        W.psc[lane][NB] = scale;
         {
             uint32_t vs[NSUB];
             int qs[NSUB], nm = 0;
@@ -512,7 +518,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             __syncwarp();
             iq_enqueue<Tr>(W, lane, nm, vs, qs, IQ_FINAL);
         }
-        iq_flush<Tr>(W, G, s_kgrid, s_c, 0, lane);
+        iq_flush<Tr>(W, G, lane);
         uint16_t fin[NSUB];
 #pragma unroll
         for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][0][q] & 0x7FFF;

@@ -11,35 +11,65 @@
 namespace qs {
 
 // ---------------------------------------------------------------------------
-// Q4_0 (kernels/q4_0.py:14-33): one thread per 32-block, HBM-bound
+// Q4_0 (kernels/q4_0.py:14-33), HBM-bound. A warp owns 32 consecutive 32-blocks
+// (2 KB of bf16) and reads them with fully coalesced 16-byte loads: in load j lane l
+// holds values [256 j + 8 l, +8), i.e. chunk l % 4 of block 8 j + l / 4, so four lanes
+// share a block (first max-abs, scale and nibble packing through shuffles).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) q4_0_kernel(QuantArgs a) {
-    constexpr int BB = 18;
-    __shared__ __align__(16) uint8_t s_out[256 * BB];
-    const int tid = threadIdx.x;
-    for (int64_t tile = blockIdx.x; tile * 256 < a.nblk; tile += gridDim.x) {
-        const int64_t b = tile * 256 + tid;
-        const int nvalid = (int)min((int64_t)256, a.nblk - tile * 256);
-        if (tid < nvalid) {
-            float x[32], amax, mx;
-            load_row<32>(a.src, b * 32, a.src_type, x);
-            absmax_first<32>(x, amax, mx);
-            const float d = __fdiv_rn(mx, -8.0f);
-            const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
-            uint8_t* o = s_out + tid * BB;
-            const uint16_t dh = f16_bits(d);
-            o[0] = (uint8_t)dh;
-            o[1] = (uint8_t)(dh >> 8);
+    constexpr int BB = 18, WARPS = 8;
+    __shared__ __align__(16) uint8_t s_out[WARPS][32 * BB];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 3;
+    uint8_t* so = s_out[warp];
+    for (int64_t wt = (int64_t)blockIdx.x * WARPS + warp; wt * 32 < a.nblk; wt += (int64_t)gridDim.x * WARPS) {
+        const int nvalid = (int)min((int64_t)32, a.nblk - wt * 32);
+        float v[4][8];
 #pragma unroll
-            for (int i = 0; i < 16; i++) {
-                int lo = (int)clampf(floorf(x[i] * id + 8.5f), 0.0f, 15.0f);
-                int hi = (int)clampf(floorf(x[16 + i] * id + 8.5f), 0.0f, 15.0f);
-                o[2 + i] = (uint8_t)(lo | (hi << 4));
+        for (int j = 0; j < 4; j++) {
+            const int blk = 8 * j + (lane >> 2);
+            if (blk < nvalid) load_row<8>(a.src, wt * 1024 + 256 * j + 8 * lane, a.src_type, v[j]);
+            else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[j][i] = 0.0f;
             }
         }
-        __syncthreads();
-        store_tile(a, s_out, tile * 256, nvalid, BB, tid, 256);
-        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int blk = 8 * j + (lane >> 2);
+            // first index of the largest |x| over the block's 4 chunks
+            float am = fabsf(v[j][0]), m = v[j][0];
+            int idx = 8 * c;
+#pragma unroll
+            for (int i = 1; i < 8; i++)
+                if (fabsf(v[j][i]) > am) { am = fabsf(v[j][i]); m = v[j][i]; idx = 8 * c + i; }
+#pragma unroll
+            for (int o = 1; o <= 2; o <<= 1) {
+                const float pa = __shfl_xor_sync(0xffffffffu, am, o), pm = __shfl_xor_sync(0xffffffffu, m, o);
+                const int pi = __shfl_xor_sync(0xffffffffu, idx, o);
+                if (pa > am || (pa == am && pi < idx)) { am = pa; m = pm; idx = pi; }
+            }
+            const float d = __fdiv_rn(m, -8.0f);
+            const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
+            uint32_t qa = 0, qb = 0;  // one level per byte
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                qa |= (uint32_t)clampf(floorf(v[j][i] * id + 8.5f), 0.0f, 15.0f) << (8 * i);
+                qb |= (uint32_t)clampf(floorf(v[j][4 + i] * id + 8.5f), 0.0f, 15.0f) << (8 * i);
+            }
+            // byte i of a block = q[i] | q[16 + i] << 4: chunk c pairs with chunk c + 2
+            const uint32_t ha = __shfl_xor_sync(0xffffffffu, qa, 2), hb = __shfl_xor_sync(0xffffffffu, qb, 2);
+            if (c < 2 && blk < nvalid) {
+                uint8_t* o = so + blk * BB;
+                const uint32_t w0 = qa | (ha << 4), w1 = qb | (hb << 4);
+                uint16_t* o16 = reinterpret_cast<uint16_t*>(o + 2 + 8 * c);
+                o16[0] = (uint16_t)w0; o16[1] = (uint16_t)(w0 >> 16);
+                o16[2] = (uint16_t)w1; o16[3] = (uint16_t)(w1 >> 16);
+                if (c == 0) *reinterpret_cast<uint16_t*>(o) = f16_bits(d);
+            }
+        }
+        __syncwarp();
+        store_tile(a, so, wt * 32, nvalid, BB, lane, 32);
+        __syncwarp();
     }
 }
 
@@ -547,7 +577,7 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
     switch (type) {
     case QS_Q4_0: {
         auto k = q4_0_kernel;
-        q4_0_kernel<<<grid_for(k, (a.nblk + 255) / 256, ctx), 256, 0, st>>>(a);
+        q4_0_kernel<<<grid_for(k, (a.nblk + 255) / 256, ctx), 256, 0, st>>>(a);  // 8 warp tiles of 32 blocks
         break;
     }
     case QS_Q4_K:
