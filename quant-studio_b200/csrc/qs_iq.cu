@@ -7,16 +7,14 @@
 // weights, the sign handling and the accept chain over the candidate scales. The grid
 // projections are where the time goes: a subgroup's tentative code is either on the
 // lattice (one table lookup) or needs a best-neighbour search over a list of 1..292
-// candidates. Lists are that uneven, so one lane per search would leave most of a warp
-// idle. Instead each warp queues its off-grid searches in shared memory (all sweep steps
-// of a batch at once: their codes depend only on the group maximum) and walks the
-// concatenated candidate stream in 32 equal slices, one per lane. A lane keeps the best
-// (d2, position) of each list it touches and merges it into the list's result with a
-// 64-bit atomicMin, which keeps the reference's first-minimum rule (strict <).
+// candidates. All sweep steps' codes depend only on the group maximum, so each warp
+// queues the off-grid searches of a batch of steps in shared memory, counting-sorts
+// them by list length, and then gives one search to each lane: the 32 lanes of a warp
+// walk lists of similar length in lockstep, with no synchronisation inside the walk.
 // The weighted distance of one candidate is a sum over positions of terms that depend
-// only on the position and the candidate's level there, so each lane first tabulates
-// the 4 x 8 (IQ2) or 8 x 4 (IQ3) terms of its current search, computed exactly as the
-// reference does, and then reads them per candidate.
+// only on the position and the candidate's level there, so a lane first tabulates the
+// 4 x 8 (IQ2) or 8 x 4 (IQ3) terms of its search, computed exactly as the reference
+// does, and then needs one table read and one add per position and candidate.
 #include <algorithm>
 #include <vector>
 
@@ -146,35 +144,30 @@ enum Reproj { RP_ALL_PROJ, RP_OFFGRID_NEED, RP_OFFGRID_REDO, RP_ALL_REDO };
 
 template <int T> struct IqT;
 template <> struct IqT<QS_IQ2_XXS> {
-    static constexpr int LPP = 32;  // lanes per neighbour search
     static constexpr int GS = 32, NSUB = 4, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 13, BB = 66, GID = G_IQ2XXS;
     static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = true;
     static constexpr int SUMK = SUM_TORCH, RP = RP_ALL_PROJ;
     static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
 };
 template <> struct IqT<QS_IQ2_XS> {
-    static constexpr int LPP = 32;  // lanes per neighbour search
     static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 74, GID = G_IQ2XS;
     static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
     static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
 };
 template <> struct IqT<QS_IQ2_S> {
-    static constexpr int LPP = 16;  // lanes per neighbour search
     static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 82, GID = G_IQ2S;
     static constexpr bool PARITY = false, ACT_GT0 = false, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
     static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 0.9875f;
 };
 template <> struct IqT<QS_IQ3_XXS> {
-    static constexpr int LPP = 8;  // lanes per neighbour search
     static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 31, BB = 98, GID = G_IQ3XXS;
     static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_REDO;
     static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 1.0125f;
 };
 template <> struct IqT<QS_IQ3_S> {
-    static constexpr int LPP = 16;  // lanes per neighbour search
     static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 19, BB = 110, GID = G_IQ3S;
     static constexpr bool PARITY = false, ACT_GT0 = true, INIT_QP = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_ALL_REDO;
@@ -189,21 +182,22 @@ struct IqParams {
 constexpr int IQ_WARPS = 4;      // warps per CTA; each warp owns 32 groups
 constexpr int IQ_CAP = 512;      // queued searches per warp
 constexpr int IQ_FINAL = 15;     // tag slot of the final reprojection
+constexpr int IQ_BINS = 80;      // length classes of the search sort (4 lengths each, last one open)
 
 template <class Tr>
 struct IqWarpSmem {
     static constexpr int NB = IQ_CAP / (32 * Tr::NSUB);  // sweep steps per batch
-    static constexpr int NS = 32 / Tr::LPP;              // searches in flight per warp
-    static constexpr int RED = 2 * 32 * (Tr::LPP + 1);
     float xv[32][Tr::GS];        // search-space values of every group (|x|, parity-folded)
     float wv[32][Tr::GS];        // sqrt of the weights
-    // sigma2 squares during the weights, then per-lane search minima [search][lane] (d2, position)
-    float scratch[RED > 1024 ? RED : 1024];
-    float tbl[32 * NS];          // distance terms of the searches in flight [position * NLEV + level][search]
+    float tbl[32][32];           // distance terms of each lane's search [position * NLEV + level][lane];
+                                 // holds the superblock squares while the weights are computed
     float psc[32][NB + 1];       // per group: search scale of each batch step, then the final scale
     uint32_t off[IQ_CAP];
     uint16_t len[IQ_CAP];
     uint16_t tag[IQ_CAP];        // group | slot << 5 | subgroup << 9
+    uint16_t ord[IQ_CAP];        // searches in order of list length
+    uint16_t rank[IQ_CAP];
+    uint32_t hist[IQ_BINS];
     uint16_t win[32][NB][Tr::NSUB];  // resolved grid index (| 0x8000 when it came from a search)
     float part[4][8];
     int nq;
@@ -225,70 +219,95 @@ __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
     return x - v;
 }
 
-// Solve every queued search of this warp: LPP lanes per search, 32/LPP searches at a
-// time. The LPP lanes first tabulate the search's distance terms (one table entry per
-// lane), then take candidates c = lane, lane + LPP, ... in list order keeping their first
-// minimum; the per-lane minima of 32 searches are transposed through shared memory and
-// lane i merges search i (smaller d2, then smaller position: the reference's argmin).
+// Solve every queued search of this warp, one search per lane, longest lists first.
 template <class Tr>
 __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
     using WS = IqWarpSmem<Tr>;
-    constexpr int LPP = Tr::LPP, NS = WS::NS, NE = Tr::NPOS * Tr::NLEV, RS = LPP + 1;
-    static_assert(NE == 32, "term table holds 32 entries");
     const int P = W.nq;
-    const int sub = lane / LPP, sl = lane % LPP;
-    float* red_d = W.scratch;
-    int* red_p = reinterpret_cast<int*>(W.scratch) + 32 * RS;
-    for (int pb = 0; pb < P; pb += 32) {
-        const int nbp = min(32, P - pb);
-        for (int k = 0; k < nbp; k += NS) {
-            const int p = pb + k + sub;
-            int len = 0;
-            uint32_t off = 0;
-            if (k + sub < nbp) {
-                off = W.off[p];
-                len = W.len[p];
-                const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
-                const float sc = W.psc[g][slot == IQ_FINAL ? WS::NB : slot];
+    // counting sort by list length (descending classes)
+    for (int i = lane; i < IQ_BINS; i += 32) W.hist[i] = 0;
+    __syncwarp();
+    for (int i = lane; i < P; i += 32) {
+        const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i] >> 2);
+        W.rank[i] = (uint16_t)atomicAdd(&W.hist[bin], 1u);
+    }
+    __syncwarp();
+    {
+        constexpr int PER = (IQ_BINS + 31) / 32;
+        int loc[PER], sum = 0;
 #pragma unroll
-                for (int e = sl; e < NE; e += LPP) {
-                    const int j = e / Tr::NLEV, l = e % Tr::NLEV;
-                    const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
-                    const float df = sc * (float)(2 * l + 1) - xj;
-                    W.tbl[e * NS + sub] = (wj * df) * df;
+        for (int k = 0; k < PER; k++) {
+            const int i = lane * PER + k;
+            loc[k] = i < IQ_BINS ? W.hist[i] : 0;
+            sum += loc[k];
+        }
+        int tot;
+        int run = warp_excl_scan(sum, lane, tot);
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < PER; k++) {
+            const int i = lane * PER + k;
+            if (i < IQ_BINS) W.hist[i] = (uint32_t)run;
+            run += loc[k];
+        }
+    }
+    __syncwarp();
+    for (int i = lane; i < P; i += 32) {
+        const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i] >> 2);
+        W.ord[W.hist[bin] + W.rank[i]] = (uint16_t)i;
+    }
+    __syncwarp();
+
+    for (int pb = 0; pb < P; pb += 32) {
+        const int i = pb + lane;
+        if (i < P) {
+            const int p = W.ord[i];
+            const uint32_t off = W.off[p];
+            const int n = W.len[p];
+            const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
+            const float sc = W.psc[g][slot == IQ_FINAL ? WS::NB : slot];
+            float sg[Tr::NLEV];
+#pragma unroll
+            for (int l = 0; l < Tr::NLEV; l++) sg[l] = sc * (float)(2 * l + 1);
+#pragma unroll
+            for (int j = 0; j < Tr::NPOS; j++) {
+                const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
+#pragma unroll
+                for (int l = 0; l < Tr::NLEV; l++) {
+                    const float df = sg[l] - xj;
+                    W.tbl[j * Tr::NLEV + l][lane] = (wj * df) * df;
                 }
             }
-            __syncwarp();
-            float bd = __int_as_float(0x7f800000);
-            int bp = 0x7fffffff;
-#pragma unroll 2
-            for (int c = sl; c < len; c += LPP) {
-                const int code = (int)(__ldg(G.list + off + c) >> 16);
-                float d2 = W.tbl[(code & (Tr::NLEV - 1)) * NS + sub];
+            const uint32_t* lp = G.list + off;
+            float bd = 0.0f;
+            int bp = -1;
+            int c = 0;
+            for (; c + 4 <= n; c += 4) {
+                uint32_t e[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) e[u] = __ldg(lp + c + u);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int code = (int)(e[u] >> 16);
+                    float d2 = W.tbl[code & (Tr::NLEV - 1)][lane];
+#pragma unroll
+                    for (int j = 1; j < Tr::NPOS; j++)
+                        d2 = __fadd_rn(d2, W.tbl[j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))][lane]);
+                    if (bp < 0 || d2 < bd) { bd = d2; bp = c + u; }
+                }
+            }
+            for (; c < n; c++) {
+                const int code = (int)(__ldg(lp + c) >> 16);
+                float d2 = W.tbl[code & (Tr::NLEV - 1)][lane];
 #pragma unroll
                 for (int j = 1; j < Tr::NPOS; j++)
-                    d2 = __fadd_rn(d2, W.tbl[(j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))) * NS + sub]);
-                if (d2 < bd || bp == 0x7fffffff) { bd = d2; bp = c; }
+                    d2 = __fadd_rn(d2, W.tbl[j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))][lane]);
+                if (bp < 0 || d2 < bd) { bd = d2; bp = c; }
             }
-            red_d[(k + sub) * RS + sl] = bd;
-            red_p[(k + sub) * RS + sl] = bp;
-            __syncwarp();
+            W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)((__ldg(lp + bp) & 0xFFFF) | 0x8000);
         }
-        if (lane < nbp) {
-            float bd = red_d[lane * RS];
-            int bp = red_p[lane * RS];
-#pragma unroll 4
-            for (int c = 1; c < LPP; c++) {
-                const float d = red_d[lane * RS + c];
-                const int pp = red_p[lane * RS + c];
-                if (d < bd || (d == bd && pp < bp)) { bd = d; bp = pp; }
-            }
-            const int p = pb + lane;
-            const int tg = W.tag[p], g = tg & 31, slot = (tg >> 5) & 15, q = tg >> 9;
-            W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)((__ldg(G.list + W.off[p] + bp) & 0xFFFF) | 0x8000);
-        }
-        __syncwarp();
     }
+    __syncwarp();
     if (lane == 0) W.nq = 0;
     __syncwarp();
 }
@@ -380,7 +399,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
 
         // weights (iq2.py:429-431, iq2_xs.py:27-29, iq2_s.py:28-30, iq3_xxs.py:40-45)
         if (IMAT) {
-            float* sq = W.scratch + sbl * QK_K;
+            float* sq = &W.tbl[0][0] + sbl * QK_K;
 #pragma unroll
             for (int i = 0; i < GS; i++) sq[gl * GS + i] = x[i] * x[i];
             __syncwarp();

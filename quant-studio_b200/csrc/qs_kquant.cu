@@ -11,65 +11,91 @@
 namespace qs {
 
 // ---------------------------------------------------------------------------
-// Q4_0 (kernels/q4_0.py:14-33), HBM-bound. A warp owns 32 consecutive 32-blocks
-// (2 KB of bf16) and reads them with fully coalesced 16-byte loads: in load j lane l
-// holds values [256 j + 8 l, +8), i.e. chunk l % 4 of block 8 j + l / 4, so four lanes
-// share a block (first max-abs, scale and nibble packing through shuffles).
+// Q4_0 (kernels/q4_0.py:14-33), HBM-bound. A warp owns tiles of 32 consecutive
+// 32-blocks. It issues every 16-byte load of U tiles before using any (fully
+// coalesced: lane l reads bytes 16 l + 512 j of a tile), parks them in shared memory,
+// and then each lane quantizes one whole block from there: no shuffles, one reciprocal
+// per block. d = max / -8 is computed as max * -0.125, which is the same IEEE result.
 // ---------------------------------------------------------------------------
+template <int ES>  // source element size in bytes
 __global__ void __launch_bounds__(256) q4_0_kernel(QuantArgs a) {
-    constexpr int BB = 18, WARPS = 8;
+    constexpr int BB = 18, WARPS = 8, TILE = 32 * 32 * ES, U = ES == 2 ? 2 : 1, NV = TILE / 512;
+    __shared__ __align__(16) uint8_t s_in[WARPS][U * TILE];
     __shared__ __align__(16) uint8_t s_out[WARPS][32 * BB];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, c = lane & 3;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* si = s_in[warp];
     uint8_t* so = s_out[warp];
-    for (int64_t wt = (int64_t)blockIdx.x * WARPS + warp; wt * 32 < a.nblk; wt += (int64_t)gridDim.x * WARPS) {
-        const int nvalid = (int)min((int64_t)32, a.nblk - wt * 32);
-        float v[4][8];
+    const uint8_t* src = static_cast<const uint8_t*>(a.src);
+    const int64_t ntile = (a.nblk + 31) / 32;
+    for (int64_t t0 = ((int64_t)blockIdx.x * WARPS + warp) * U; t0 < ntile; t0 += (int64_t)gridDim.x * WARPS * U) {
+        uint4 r[U][NV];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int blk = 8 * j + (lane >> 2);
-            if (blk < nvalid) load_row<8>(a.src, wt * 1024 + 256 * j + 8 * lane, a.src_type, v[j]);
-            else {
+        for (int u = 0; u < U; u++) {
+            const int64_t base = (t0 + u) * TILE;
+            const int64_t lim = a.nblk * 32 * ES;  // bytes of input
 #pragma unroll
-                for (int i = 0; i < 8; i++) v[j][i] = 0.0f;
+            for (int j = 0; j < NV; j++) {
+                const int64_t off = base + 512 * j + 16 * lane;
+                r[u][j] = off < lim ? __ldg(reinterpret_cast<const uint4*>(src + off)) : make_uint4(0, 0, 0, 0);
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int blk = 8 * j + (lane >> 2);
-            // first index of the largest |x| over the block's 4 chunks
-            float am = fabsf(v[j][0]), m = v[j][0];
-            int idx = 8 * c;
+        for (int u = 0; u < U; u++)
 #pragma unroll
-            for (int i = 1; i < 8; i++)
-                if (fabsf(v[j][i]) > am) { am = fabsf(v[j][i]); m = v[j][i]; idx = 8 * c + i; }
+            for (int j = 0; j < NV; j++) *reinterpret_cast<uint4*>(si + u * TILE + 512 * j + 16 * lane) = r[u][j];
+        __syncwarp();
 #pragma unroll
-            for (int o = 1; o <= 2; o <<= 1) {
-                const float pa = __shfl_xor_sync(0xffffffffu, am, o), pm = __shfl_xor_sync(0xffffffffu, m, o);
-                const int pi = __shfl_xor_sync(0xffffffffu, idx, o);
-                if (pa > am || (pa == am && pi < idx)) { am = pa; m = pm; idx = pi; }
-            }
-            const float d = __fdiv_rn(m, -8.0f);
-            const float id = d != 0.0f ? rcp_rn(d) : 0.0f;
-            uint32_t qa = 0, qb = 0;  // one level per byte
+        for (int u = 0; u < U; u++) {
+            const int64_t tile = t0 + u;
+            if (tile >= ntile) break;
+            const int nvalid = (int)min((int64_t)32, a.nblk - tile * 32);
+            float x[32];
+            const uint8_t* blk = si + u * TILE + lane * 32 * ES;
+            if (ES == 4) {
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                qa |= (uint32_t)clampf(floorf(v[j][i] * id + 8.5f), 0.0f, 15.0f) << (8 * i);
-                qb |= (uint32_t)clampf(floorf(v[j][4 + i] * id + 8.5f), 0.0f, 15.0f) << (8 * i);
+                for (int i = 0; i < 8; i++) {
+                    const float4 f = reinterpret_cast<const float4*>(blk)[i];
+                    x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const uint4 t = reinterpret_cast<const uint4*>(blk)[i];
+                    const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int h = 0; h < 4; h++) {
+                        const uint32_t lo = w4[h] & 0xFFFFu, hi = w4[h] >> 16;
+                        if (a.src_type == SRC_BF16) {
+                            x[8 * i + 2 * h] = __uint_as_float(lo << 16);
+                            x[8 * i + 2 * h + 1] = __uint_as_float(hi << 16);
+                        } else {
+                            x[8 * i + 2 * h] = __half2float(__ushort_as_half((unsigned short)lo));
+                            x[8 * i + 2 * h + 1] = __half2float(__ushort_as_half((unsigned short)hi));
+                        }
+                    }
+                }
             }
-            // byte i of a block = q[i] | q[16 + i] << 4: chunk c pairs with chunk c + 2
-            const uint32_t ha = __shfl_xor_sync(0xffffffffu, qa, 2), hb = __shfl_xor_sync(0xffffffffu, qb, 2);
-            if (c < 2 && blk < nvalid) {
-                uint8_t* o = so + blk * BB;
-                const uint32_t w0 = qa | (ha << 4), w1 = qb | (hb << 4);
-                uint16_t* o16 = reinterpret_cast<uint16_t*>(o + 2 + 8 * c);
-                o16[0] = (uint16_t)w0; o16[1] = (uint16_t)(w0 >> 16);
-                o16[2] = (uint16_t)w1; o16[3] = (uint16_t)(w1 >> 16);
-                if (c == 0) *reinterpret_cast<uint16_t*>(o) = f16_bits(d);
+            float am, m;
+            absmax_first<32>(x, am, m);
+            const float d = m * -0.125f;
+            const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+            uint32_t wq[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const uint32_t lo = (uint32_t)clampf(floorf(x[i] * id + 8.5f), 0.0f, 15.0f);
+                const uint32_t hi = (uint32_t)clampf(floorf(x[16 + i] * id + 8.5f), 0.0f, 15.0f);
+                wq[i >> 2] |= (lo | (hi << 4)) << (8 * (i & 3));
             }
+            if (lane < nvalid) {
+                uint16_t* o16 = reinterpret_cast<uint16_t*>(so + lane * BB);
+                o16[0] = f16_bits(d);
+#pragma unroll
+                for (int i = 0; i < 4; i++) { o16[1 + 2 * i] = (uint16_t)wq[i]; o16[2 + 2 * i] = (uint16_t)(wq[i] >> 16); }
+            }
+            __syncwarp();
+            store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
+            __syncwarp();
         }
-        __syncwarp();
-        store_tile(a, so, wt * 32, nvalid, BB, lane, 32);
-        __syncwarp();
     }
 }
 
@@ -576,8 +602,14 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
     cudaStream_t st = ctx.stream;
     switch (type) {
     case QS_Q4_0: {
-        auto k = q4_0_kernel;
-        q4_0_kernel<<<grid_for(k, (a.nblk + 255) / 256, ctx), 256, 0, st>>>(a);  // 8 warp tiles of 32 blocks
+        const int64_t ctas = (a.nblk + 511) / 512;  // 8 warps x 2 tiles of 32 blocks
+        if (a.src_type == SRC_F32) {
+            auto k = q4_0_kernel<4>;
+            q4_0_kernel<4><<<grid_for(k, ctas, ctx), 256, 0, st>>>(a);
+        } else {
+            auto k = q4_0_kernel<2>;
+            q4_0_kernel<2><<<grid_for(k, ctas, ctx), 256, 0, st>>>(a);
+        }
         break;
     }
     case QS_Q4_K:
