@@ -293,7 +293,10 @@ def main() -> None:
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic (seeded, generated on device; random-init weights of the config shapes)",
             "config": config, "roofline": roof, "clocks": clocks, "gpu_launches": args.steps * len(xs),
-            "kernel_ms_per_launch": round(launch_ms, 4), "e2e": e2e}
+            "kernel_ms_per_launch": round(launch_ms, 4),
+            "kernel_ms_by_shape": {f"{r}x{c}": round(statistics.median(k[i] for k in kern_ms), 4)
+                                   for i, (r, c) in enumerate(SHAPES_C2) if i in (0, len(SHAPES_C2) - 1)},
+            "e2e": e2e}
     if rank == 0 and world == 1 and args.cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args)
     if dist is not None:

@@ -179,17 +179,18 @@ struct IqParams {
     float qp[8];   // make_qp numerators (IQ2_XXS initial scale)
 };
 
-constexpr int IQ_WARPS = 4;      // warps per CTA; each warp owns 32 groups
-constexpr int IQ_CAP = 512;      // queued searches per warp
+constexpr int IQ_WARPS = 2;      // warps per CTA; each warp owns 32 groups
+constexpr int IQ_CAP = 256;      // queued searches per warp
 constexpr int IQ_FINAL = 15;     // tag slot of the final reprojection
-constexpr int IQ_BINS = 80;      // length classes of the search sort (4 lengths each, last one open)
+constexpr int IQ_BINS = 293;     // list lengths 1..292 (the longest IQ2_XS list)
 
 template <class Tr>
 struct IqWarpSmem {
     static constexpr int NB = IQ_CAP / (32 * Tr::NSUB);  // sweep steps per batch
-    float xv[32][Tr::GS];        // search-space values of every group (|x|, parity-folded)
-    float wv[32][Tr::GS];        // sqrt of the weights
-    float tbl[32][32];           // distance terms of each lane's search [position * NLEV + level][lane];
+    static constexpr int NT = Tr::NPOS == 8 ? 16 + 6 * 4 : 32;  // IQ2: pair table of positions 0,1 + 6 x 4
+    float xv[32][Tr::GS + 1];    // search-space values of every group (|x|, parity-folded); +1: no bank clash
+    float wv[32][Tr::GS + 1];    // sqrt of the weights
+    float tbl[NT > 32 ? NT : 32][32];  // distance terms of each lane's search [entry][lane];
                                  // holds the superblock squares while the weights are computed
     float psc[32][NB + 1];       // per group: search scale of each batch step, then the final scale
     uint32_t off[IQ_CAP];
@@ -197,7 +198,7 @@ struct IqWarpSmem {
     uint16_t tag[IQ_CAP];        // group | slot << 5 | subgroup << 9
     uint16_t ord[IQ_CAP];        // searches in order of list length
     uint16_t rank[IQ_CAP];
-    uint32_t hist[IQ_BINS];
+    uint32_t hist[(IQ_BINS + 1) / 2];  // two 16-bit counters (then bin starts) per word
     uint16_t win[32][NB][Tr::NSUB];  // resolved grid index (| 0x8000 when it came from a search)
     float part[4][8];
     int nq;
@@ -205,7 +206,7 @@ struct IqWarpSmem {
 
 template <class Tr>
 constexpr size_t iq_smem_bytes() {
-    return IQ_WARPS * sizeof(IqWarpSmem<Tr>) + 1024 * 2 + 64 * 4 + 16 * Tr::BB + 64;
+    return IQ_WARPS * sizeof(IqWarpSmem<Tr>) + 64 * 4 + IQ_WARPS * 4 * Tr::BB + 64;
 }
 
 __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
@@ -224,37 +225,38 @@ template <class Tr>
 __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
     using WS = IqWarpSmem<Tr>;
     const int P = W.nq;
-    // counting sort by list length (descending classes)
-    for (int i = lane; i < IQ_BINS; i += 32) W.hist[i] = 0;
+    // counting sort by list length, longest first
+    constexpr int HW = (IQ_BINS + 1) / 2, PER = 2 * ((HW + 31) / 32);  // bins per lane (even)
+    for (int i = lane; i < HW; i += 32) W.hist[i] = 0;
     __syncwarp();
     for (int i = lane; i < P; i += 32) {
-        const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i] >> 2);
-        W.rank[i] = (uint16_t)atomicAdd(&W.hist[bin], 1u);
+        const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i]);
+        const int sh = 16 * (bin & 1);
+        W.rank[i] = (uint16_t)((atomicAdd(&W.hist[bin >> 1], 1u << sh) >> sh) & 0xFFFF);
     }
     __syncwarp();
     {
-        constexpr int PER = (IQ_BINS + 31) / 32;
-        int loc[PER], sum = 0;
+        int cnt[PER], sum = 0;
 #pragma unroll
         for (int k = 0; k < PER; k++) {
-            const int i = lane * PER + k;
-            loc[k] = i < IQ_BINS ? W.hist[i] : 0;
-            sum += loc[k];
+            const int b = lane * PER + k;
+            cnt[k] = b < IQ_BINS ? (int)((W.hist[b >> 1] >> (16 * (b & 1))) & 0xFFFF) : 0;
+            sum += cnt[k];
         }
         int tot;
         int run = warp_excl_scan(sum, lane, tot);
         __syncwarp();
 #pragma unroll
-        for (int k = 0; k < PER; k++) {
-            const int i = lane * PER + k;
-            if (i < IQ_BINS) W.hist[i] = (uint32_t)run;
-            run += loc[k];
+        for (int k = 0; k < PER; k += 2) {
+            const int b = lane * PER + k;
+            if (b < IQ_BINS) W.hist[b >> 1] = (uint32_t)run | ((uint32_t)(run + cnt[k]) << 16);
+            run += cnt[k] + cnt[k + 1];
         }
     }
     __syncwarp();
     for (int i = lane; i < P; i += 32) {
-        const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i] >> 2);
-        W.ord[W.hist[bin] + W.rank[i]] = (uint16_t)i;
+        const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i]);
+        W.ord[((W.hist[bin >> 1] >> (16 * (bin & 1))) & 0xFFFF) + W.rank[i]] = (uint16_t)i;
     }
     __syncwarp();
 
@@ -269,18 +271,53 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
             float sg[Tr::NLEV];
 #pragma unroll
             for (int l = 0; l < Tr::NLEV; l++) sg[l] = sc * (float)(2 * l + 1);
-#pragma unroll
-            for (int j = 0; j < Tr::NPOS; j++) {
-                const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
-#pragma unroll
-                for (int l = 0; l < Tr::NLEV; l++) {
-                    const float df = sg[l] - xj;
-                    W.tbl[j * Tr::NLEV + l][lane] = (wj * df) * df;
-                }
-            }
             const uint32_t* lp = G.list + off;
             float bd = 0.0f;
             int bp = -1;
+            if (Tr::NPOS == 8) {
+                // terms t_j(l) = (wv_j * (sc v_l - xv_j)) * (sc v_l - xv_j); the sum runs from
+                // position 0, so t_0 + t_1 is one table (16 entries), then 6 x 4 entries
+                float t0[4], t1[4];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const float xj = W.xv[g][q * 8 + j], wj = W.wv[g][q * 8 + j];
+#pragma unroll
+                    for (int l = 0; l < 4; l++) {
+                        const float df = sg[l] - xj;
+                        const float t = (wj * df) * df;
+                        if (j == 0) t0[l] = t;
+                        else if (j == 1) t1[l] = t;
+                        else W.tbl[16 + (j - 2) * 4 + l][lane] = t;
+                    }
+                }
+#pragma unroll
+                for (int l1 = 0; l1 < 4; l1++)
+#pragma unroll
+                    for (int l0 = 0; l0 < 4; l0++) W.tbl[l0 + 4 * l1][lane] = t0[l0] + t1[l1];
+            } else {
+#pragma unroll
+                for (int j = 0; j < Tr::NPOS; j++) {
+                    const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
+#pragma unroll
+                    for (int l = 0; l < Tr::NLEV; l++) {
+                        const float df = sg[l] - xj;
+                        W.tbl[j * Tr::NLEV + l][lane] = (wj * df) * df;
+                    }
+                }
+            }
+            auto dist = [&](int code) -> float {
+                if (Tr::NPOS == 8) {
+                    float d2 = W.tbl[code & 15][lane];
+#pragma unroll
+                    for (int j = 2; j < 8; j++) d2 = __fadd_rn(d2, W.tbl[16 + (j - 2) * 4 + ((code >> (2 * j)) & 3)][lane]);
+                    return d2;
+                } else {
+                    float d2 = W.tbl[code & 7][lane];
+#pragma unroll
+                    for (int j = 1; j < 4; j++) d2 = __fadd_rn(d2, W.tbl[j * 8 + ((code >> (3 * j)) & 7)][lane]);
+                    return d2;
+                }
+            };
             int c = 0;
             for (; c + 4 <= n; c += 4) {
                 uint32_t e[4];
@@ -288,20 +325,12 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
                 for (int u = 0; u < 4; u++) e[u] = __ldg(lp + c + u);
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const int code = (int)(e[u] >> 16);
-                    float d2 = W.tbl[code & (Tr::NLEV - 1)][lane];
-#pragma unroll
-                    for (int j = 1; j < Tr::NPOS; j++)
-                        d2 = __fadd_rn(d2, W.tbl[j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))][lane]);
+                    const float d2 = dist((int)(e[u] >> 16));
                     if (bp < 0 || d2 < bd) { bd = d2; bp = c + u; }
                 }
             }
             for (; c < n; c++) {
-                const int code = (int)(__ldg(lp + c) >> 16);
-                float d2 = W.tbl[code & (Tr::NLEV - 1)][lane];
-#pragma unroll
-                for (int j = 1; j < Tr::NPOS; j++)
-                    d2 = __fadd_rn(d2, W.tbl[j * Tr::NLEV + ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))][lane]);
+                const float d2 = dist((int)(__ldg(lp + c) >> 16));
                 if (bp < 0 || d2 < bd) { bd = d2; bp = c; }
             }
             W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)((__ldg(lp + bp) & 0xFFFF) | 0x8000);
@@ -344,10 +373,10 @@ __device__ __forceinline__ void iq_enqueue(IqWarpSmem<Tr>& W, int lane, int nmin
 
 // grid values (2l+1) of the winners of one group -> q[GS]
 template <class Tr>
-__device__ __forceinline__ void iq_decode(const uint16_t* s_kgrid, const uint16_t* win, float* q) {
+__device__ __forceinline__ void iq_decode(const uint16_t* kgrid, const uint16_t* win, float* q) {
 #pragma unroll
     for (int s = 0; s < Tr::NSUB; s++) {
-        const int code = s_kgrid[win[s] & 0x7FFF];
+        const int code = __ldg(kgrid + (win[s] & 0x7FFF));
 #pragma unroll
         for (int j = 0; j < Tr::NPOS; j++) q[s * Tr::NPOS + j] = (float)(2 * ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1)) + 1);
     }
@@ -378,14 +407,12 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
     constexpr int NB = WS::NB;
     extern __shared__ __align__(16) unsigned char smem[];
     WS* wsm = reinterpret_cast<WS*>(smem);
-    uint16_t* s_kgrid = reinterpret_cast<uint16_t*>(smem + IQ_WARPS * sizeof(WS));
-    float* s_c = reinterpret_cast<float*>(s_kgrid + 1024);
+    float* s_c = reinterpret_cast<float*>(smem + IQ_WARPS * sizeof(WS));
     float* s_qp = s_c + 32;
     uint8_t* s_out = reinterpret_cast<uint8_t*>(s_qp + 32);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     WS& W = wsm[warp];
-    for (int i = tid; i < G.grid; i += blockDim.x) s_kgrid[i] = G.kgrid[i];
     if (tid < 32) s_c[tid] = prm.c[tid];
     if (tid < 8) s_qp[tid] = prm.qp[tid];
     if (lane == 0) W.nq = 0;
@@ -491,7 +518,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             iq_flush<Tr>(W, G, lane);
             for (int j = 0; j < nb; j++) {
                 float qv[GS], sumqx, sumq2;
-                iq_decode<Tr>(s_kgrid, W.win[lane][j], qv);
+                iq_decode<Tr>(G.kgrid, W.win[lane][j], qv);
                 iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
                 if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
                     const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
@@ -543,7 +570,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
         for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][0][q] & 0x7FFF;
         {
             float qv[GS], sumqx, sumq2;
-            iq_decode<Tr>(s_kgrid, fin, qv);
+            iq_decode<Tr>(G.kgrid, fin, qv);
             iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
             if (redo && sumq2 > 0.0f) scale = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
         }

@@ -12,90 +12,104 @@ namespace qs {
 
 // ---------------------------------------------------------------------------
 // Q4_0 (kernels/q4_0.py:14-33), HBM-bound. A warp owns tiles of 32 consecutive
-// 32-blocks. It issues every 16-byte load of U tiles before using any (fully
-// coalesced: lane l reads bytes 16 l + 512 j of a tile), parks them in shared memory,
-// and then each lane quantizes one whole block from there: no shuffles, one reciprocal
-// per block. d = max / -8 is computed as max * -0.125, which is the same IEEE result.
+// 32-blocks, read with fully coalesced 16-byte loads (lane l: bytes 16 l + 512 j of the
+// tile). The loads of the warp's next tile are issued before the current tile is
+// quantized, so memory stays busy while the warp computes. Tiles are parked in shared
+// memory and each lane quantizes one whole block from there: no shuffles, one
+// reciprocal per block. d = max / -8 is computed as max * -0.125 (the same IEEE value).
 // ---------------------------------------------------------------------------
 template <int ES>  // source element size in bytes
 __global__ void __launch_bounds__(256) q4_0_kernel(QuantArgs a) {
-    constexpr int BB = 18, WARPS = 8, TILE = 32 * 32 * ES, U = ES == 2 ? 2 : 1, NV = TILE / 512;
-    __shared__ __align__(16) uint8_t s_in[WARPS][U * TILE];
+    constexpr int BB = 18, WARPS = 8, TILE = 32 * 32 * ES, NV = TILE / 512;
+    __shared__ __align__(16) uint8_t s_in[WARPS][TILE];
     __shared__ __align__(16) uint8_t s_out[WARPS][32 * BB];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint8_t* si = s_in[warp];
     uint8_t* so = s_out[warp];
     const uint8_t* src = static_cast<const uint8_t*>(a.src);
-    const int64_t ntile = (a.nblk + 31) / 32;
-    for (int64_t t0 = ((int64_t)blockIdx.x * WARPS + warp) * U; t0 < ntile; t0 += (int64_t)gridDim.x * WARPS * U) {
-        uint4 r[U][NV];
+    const int64_t ntile = (a.nblk + 31) / 32, lim = a.nblk * 32 * ES;
+    const int64_t stride = (int64_t)gridDim.x * WARPS;
+    int64_t tile = (int64_t)blockIdx.x * WARPS + warp;
+    uint4 r[NV];
+    auto fetch = [&](int64_t t) {
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int64_t base = (t0 + u) * TILE;
-            const int64_t lim = a.nblk * 32 * ES;  // bytes of input
-#pragma unroll
-            for (int j = 0; j < NV; j++) {
-                const int64_t off = base + 512 * j + 16 * lane;
-                r[u][j] = off < lim ? __ldg(reinterpret_cast<const uint4*>(src + off)) : make_uint4(0, 0, 0, 0);
-            }
+        for (int j = 0; j < NV; j++) {
+            const int64_t off = t * TILE + 512 * j + 16 * lane;
+            r[j] = (t < ntile && off < lim) ? __ldg(reinterpret_cast<const uint4*>(src + off)) : make_uint4(0, 0, 0, 0);
         }
+    };
+    fetch(tile);
+    for (; tile < ntile; tile += stride) {
 #pragma unroll
-        for (int u = 0; u < U; u++)
-#pragma unroll
-            for (int j = 0; j < NV; j++) *reinterpret_cast<uint4*>(si + u * TILE + 512 * j + 16 * lane) = r[u][j];
+        for (int j = 0; j < NV; j++) *reinterpret_cast<uint4*>(si + 512 * j + 16 * lane) = r[j];
         __syncwarp();
+        fetch(tile + stride);
+        const int nvalid = (int)min((int64_t)32, a.nblk - tile * 32);
+        float x[32];
+        const uint8_t* blk = si + lane * 32 * ES;
+        if (ES == 4) {
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int64_t tile = t0 + u;
-            if (tile >= ntile) break;
-            const int nvalid = (int)min((int64_t)32, a.nblk - tile * 32);
-            float x[32];
-            const uint8_t* blk = si + u * TILE + lane * 32 * ES;
-            if (ES == 4) {
+            for (int i = 0; i < 8; i++) {
+                const float4 f = reinterpret_cast<const float4*>(blk)[i];
+                x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
+            }
+        } else {
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float4 f = reinterpret_cast<const float4*>(blk)[i];
-                    x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
-                }
-            } else {
+            for (int i = 0; i < 4; i++) {
+                const uint4 t = reinterpret_cast<const uint4*>(blk)[i];
+                const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint4 t = reinterpret_cast<const uint4*>(blk)[i];
-                    const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                    for (int h = 0; h < 4; h++) {
-                        const uint32_t lo = w4[h] & 0xFFFFu, hi = w4[h] >> 16;
-                        if (a.src_type == SRC_BF16) {
-                            x[8 * i + 2 * h] = __uint_as_float(lo << 16);
-                            x[8 * i + 2 * h + 1] = __uint_as_float(hi << 16);
-                        } else {
-                            x[8 * i + 2 * h] = __half2float(__ushort_as_half((unsigned short)lo));
-                            x[8 * i + 2 * h + 1] = __half2float(__ushort_as_half((unsigned short)hi));
-                        }
+                for (int h = 0; h < 4; h++) {
+                    const uint32_t lo = w4[h] & 0xFFFFu, hi = w4[h] >> 16;
+                    if (a.src_type == SRC_BF16) {
+                        x[8 * i + 2 * h] = __uint_as_float(lo << 16);
+                        x[8 * i + 2 * h + 1] = __uint_as_float(hi << 16);
+                    } else {
+                        x[8 * i + 2 * h] = __half2float(__ushort_as_half((unsigned short)lo));
+                        x[8 * i + 2 * h + 1] = __half2float(__ushort_as_half((unsigned short)hi));
                     }
                 }
             }
-            float am, m;
-            absmax_first<32>(x, am, m);
-            const float d = m * -0.125f;
-            const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-            uint32_t wq[4] = {0, 0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const uint32_t lo = (uint32_t)clampf(floorf(x[i] * id + 8.5f), 0.0f, 15.0f);
-                const uint32_t hi = (uint32_t)clampf(floorf(x[16 + i] * id + 8.5f), 0.0f, 15.0f);
-                wq[i >> 2] |= (lo | (hi << 4)) << (8 * (i & 3));
-            }
-            if (lane < nvalid) {
-                uint16_t* o16 = reinterpret_cast<uint16_t*>(so + lane * BB);
-                o16[0] = f16_bits(d);
-#pragma unroll
-                for (int i = 0; i < 4; i++) { o16[1 + 2 * i] = (uint16_t)wq[i]; o16[2 + 2 * i] = (uint16_t)(wq[i] >> 16); }
-            }
-            __syncwarp();
-            store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
-            __syncwarp();
         }
+        // signed value of the first largest |x|: max and min of the block decide it
+        // unless both +amax and -amax occur, then the first one in order wins
+        float mx = x[0], mn = x[0];
+#pragma unroll
+        for (int i = 1; i < 32; i++) { mx = fmaxf(mx, x[i]); mn = fminf(mn, x[i]); }
+        float m = mx > -mn ? mx : mn;
+        if (mx == -mn) {
+            float am;
+            absmax_first<32>(x, am, m);
+        }
+        const float d = m * -0.125f;
+        const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+        // q = clamp(floor(x * id + 8.5), 0, 15). |x * id| <= 8 (plus rounding), so
+        // v = x * id + 8.5 lies in (0, 17): adding 2^23 rounding toward -inf gives the
+        // float 2^23 + floor(v), whose low byte is floor(v) (0..16). Bytes of four values
+        // are gathered with byte permutes and clamped to 15 with one SIMD byte min.
+        uint32_t fb[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) fb[i] = (uint32_t)__float_as_int(__fadd_rd(x[i] * id + 8.5f, 8388608.0f));
+        uint32_t wq[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t lo = __vminu4(__byte_perm(__byte_perm(fb[4 * k], fb[4 * k + 1], 0x0040),
+                                                     __byte_perm(fb[4 * k + 2], fb[4 * k + 3], 0x0040), 0x5410),
+                                         0x0F0F0F0Fu);
+            const uint32_t hi = __vminu4(__byte_perm(__byte_perm(fb[16 + 4 * k], fb[17 + 4 * k], 0x0040),
+                                                     __byte_perm(fb[18 + 4 * k], fb[19 + 4 * k], 0x0040), 0x5410),
+                                         0x0F0F0F0Fu);
+            wq[k] = lo | (hi << 4);
+        }
+        if (lane < nvalid) {
+            uint16_t* o16 = reinterpret_cast<uint16_t*>(so + lane * BB);
+            o16[0] = f16_bits(d);
+#pragma unroll
+            for (int i = 0; i < 4; i++) { o16[1 + 2 * i] = (uint16_t)wq[i]; o16[2 + 2 * i] = (uint16_t)(wq[i] >> 16); }
+        }
+        __syncwarp();
+        store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
+        __syncwarp();
     }
 }
 
@@ -602,7 +616,7 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
     cudaStream_t st = ctx.stream;
     switch (type) {
     case QS_Q4_0: {
-        const int64_t ctas = (a.nblk + 511) / 512;  // 8 warps x 2 tiles of 32 blocks
+        const int64_t ctas = (a.nblk + 255) / 256;  // 8 warps x tiles of 32 blocks
         if (a.src_type == SRC_F32) {
             auto k = q4_0_kernel<4>;
             q4_0_kernel<4><<<grid_for(k, ctas, ctx), 256, 0, st>>>(a);
