@@ -107,6 +107,16 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def max_over_ranks(dist, value: float, device) -> float:
+    """The slowest rank's time: every rank takes the same all_reduce(MAX) step."""
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def make_inputs(torch, device, seed: int, shapes):
     """Seeded synthetic bf16 weights + lognormal imatrix, generated on the device."""
     g = torch.Generator(device=device)
@@ -247,11 +257,7 @@ def main() -> None:
     launch_ms = sum(sum(k) for k in kern_ms) / (args.steps * len(xs))
 
     def allmax(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return max_over_ranks(dist, v, device)
 
     ms_total = allmax(ms_total)
     ms_step = ms_total / args.steps

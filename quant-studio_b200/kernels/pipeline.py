@@ -91,51 +91,45 @@ class ShardedQuantizer:
                 yield j, r0, min(n, r0 + step)
 
     # -- one GPU -----------------------------------------------------------
-    def _worker(self, device: torch.device, work: queue.Queue, lock: threading.Lock):
-        try:
-            torch.cuda.set_device(device)
-            slots = [_Slot(device), _Slot(device)]
-            qw_cache: dict[int, torch.Tensor] = {}
-            s = 0
-            while self.error is None:
-                item = work.get()
-                if item is None:
-                    break
-                job, r0, r1 = item
-                slot = slots[s]
-                s ^= 1
-                self._retire(slot)
-                n = r1 - r0
-                in_bytes = n * job.rows.shape[1]
-                out_bytes = n * job.row_bytes
-                slot.h_in = _Slot._grow_pinned(slot.h_in, in_bytes)
-                slot.h_out = _Slot._grow_pinned(slot.h_out, out_bytes)
-                slot.d_in = _Slot._grow_dev(slot.d_in, in_bytes, device)
-                slot.d_out = _Slot._grow_dev(slot.d_out, out_bytes, device)
-                np.copyto(slot.h_in[:in_bytes].numpy().reshape(n, -1), job.rows[r0:r1])
-                qw = None
-                if job.qw is not None:
-                    key = id(job)
-                    if key not in qw_cache:
-                        qw_cache.clear()
-                        qw_cache[key] = torch.from_numpy(np.ascontiguousarray(job.qw[:job.k], dtype=np.float32)).to(device)
-                    qw = qw_cache[key]
-                with torch.cuda.stream(slot.stream):
-                    if qw is not None:
-                        slot.stream.wait_stream(torch.cuda.current_stream(device))
-                    slot.d_in[:in_bytes].copy_(slot.h_in[:in_bytes], non_blocking=True)
-                    x = slot.d_in[:in_bytes].view(job.src_dtype).view(n, job.k)
-                    out = slot.d_out[:out_bytes].view(n, job.row_bytes)
-                    _native.quantize_into(job.ggml_type, x, qw, out, slot.stream)
-                    slot.h_out[:out_bytes].copy_(slot.d_out[:out_bytes], non_blocking=True)
-                    slot.event.record(slot.stream)
-                slot.pending = (out_bytes, job.out_offset + r0 * job.row_bytes)
-                with lock:
-                    self.stats[job.name] = self.stats.get(job.name, 0) + n
-            for slot in slots:
-                self._retire(slot)
-        except BaseException as e:  # surfaced by run()
-            self.error = e
+    def _open(self, device: torch.device):
+        torch.cuda.set_device(device)
+        return {"device": device, "slots": [_Slot(device), _Slot(device)], "next": 0, "qw": {}}
+
+    def _submit(self, ctx, job: QuantJob, r0: int, r1: int):
+        """Stage rows r0:r1 of `job`, run the kernel, start the copy back (asynchronous)."""
+        device = ctx["device"]
+        slot = ctx["slots"][ctx["next"]]
+        ctx["next"] ^= 1
+        self._retire(slot)
+        n = r1 - r0
+        in_bytes = n * job.rows.shape[1]
+        out_bytes = n * job.row_bytes
+        slot.h_in = _Slot._grow_pinned(slot.h_in, in_bytes)
+        slot.h_out = _Slot._grow_pinned(slot.h_out, out_bytes)
+        slot.d_in = _Slot._grow_dev(slot.d_in, in_bytes, device)
+        slot.d_out = _Slot._grow_dev(slot.d_out, out_bytes, device)
+        np.copyto(slot.h_in[:in_bytes].numpy().reshape(n, -1), job.rows[r0:r1])
+        qw = None
+        if job.qw is not None:
+            cache = ctx["qw"]
+            if id(job) not in cache:
+                cache.clear()
+                cache[id(job)] = torch.from_numpy(np.ascontiguousarray(job.qw[:job.k], dtype=np.float32)).to(device)
+            qw = cache[id(job)]
+        with torch.cuda.stream(slot.stream):
+            if qw is not None:
+                slot.stream.wait_stream(torch.cuda.current_stream(device))
+            slot.d_in[:in_bytes].copy_(slot.h_in[:in_bytes], non_blocking=True)
+            x = slot.d_in[:in_bytes].view(job.src_dtype).view(n, job.k)
+            out = slot.d_out[:out_bytes].view(n, job.row_bytes)
+            _native.quantize_into(job.ggml_type, x, qw, out, slot.stream)
+            slot.h_out[:out_bytes].copy_(slot.d_out[:out_bytes], non_blocking=True)
+            slot.event.record(slot.stream)
+        slot.pending = (out_bytes, job.out_offset + r0 * job.row_bytes)
+
+    def _drain(self, ctx):
+        for slot in ctx["slots"]:
+            self._retire(slot)
 
     def _retire(self, slot: _Slot):
         """Wait for the slot's chunk and write its blocks to the file."""
@@ -143,11 +137,29 @@ class ShardedQuantizer:
             return
         nbytes, off = slot.pending
         slot.event.synchronize()
-        mv = memoryview(slot.h_out[:nbytes].numpy())
-        done = 0
-        while done < nbytes:
-            done += os.pwrite(self.fd, mv[done:], off + done)
+        self._write(slot.h_out[:nbytes].numpy(), off)
         slot.pending = None
+
+    def _write(self, buf: np.ndarray, off: int):
+        mv = memoryview(buf.reshape(-1).view(np.uint8))
+        done = 0
+        while done < len(mv):
+            done += os.pwrite(self.fd, mv[done:done + (64 << 20)], off + done)
+
+    def _worker(self, device, work: queue.Queue, lock: threading.Lock):
+        try:
+            ctx = self._open(device)
+            while self.error is None:
+                item = work.get()
+                if item is None:
+                    break
+                job, r0, r1 = item
+                self._submit(ctx, job, r0, r1)
+                with lock:
+                    self.stats[job.name] = self.stats.get(job.name, 0) + (r1 - r0)
+            self._drain(ctx)
+        except BaseException as e:  # surfaced by run()
+            self.error = e
 
     # -- driver ------------------------------------------------------------
     def run(self, jobs: list[QuantJob], copies: list[CopyJob] = ()) -> float:
@@ -162,10 +174,7 @@ class ShardedQuantizer:
         for t in threads:
             t.start()
         for c in copies:  # passthroughs on this thread while the GPUs work
-            mv = memoryview(np.ascontiguousarray(c.data).reshape(-1).view(np.uint8))
-            done = 0
-            while done < len(mv):
-                done += os.pwrite(self.fd, mv[done:done + (64 << 20)], c.out_offset + done)
+            self._write(np.ascontiguousarray(c.data), c.out_offset)
         for t in threads:
             t.join()
         if self.error is not None:
