@@ -212,17 +212,21 @@ struct QuantArgs {
 };
 
 // Copy the packed output of blocks [b0, b0 + nb) from shared memory to the rows
-// they belong to; rows may be strided in the destination.
+// they belong to; rows may be strided in the destination (then, and only then, the
+// block index is split into row and column: a 64-bit division).
 __device__ __forceinline__ void store_tile(const QuantArgs& a, const uint8_t* stage, int64_t b0, int nb,
                                            int block_bytes, int tid, int nthreads) {
+    if (a.dst_row_bytes == a.row_bytes) {
+        store_bytes(a.dst + b0 * block_bytes, stage, nb * block_bytes, tid, nthreads);
+        return;
+    }
     int64_t b = b0;
     int done = 0;
     while (done < nb) {
-        int64_t row = b / a.nblk_row, col = b - row * a.nblk_row;
-        int run = (int)min((int64_t)(nb - done), a.nblk_row - col);
-        if (a.dst_row_bytes == a.row_bytes) run = nb - done;  // contiguous rows: one run
-        uint8_t* d = a.dst + row * a.dst_row_bytes + col * block_bytes;
-        store_bytes(d, stage + (size_t)done * block_bytes, run * block_bytes, tid, nthreads);
+        const int64_t row = b / a.nblk_row, col = b - row * a.nblk_row;
+        const int run = (int)min((int64_t)(nb - done), a.nblk_row - col);
+        store_bytes(a.dst + row * a.dst_row_bytes + col * block_bytes, stage + (size_t)done * block_bytes,
+                    run * block_bytes, tid, nthreads);
         done += run;
         b += run;
     }

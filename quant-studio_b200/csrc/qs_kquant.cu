@@ -12,70 +12,103 @@ namespace qs {
 
 // ---------------------------------------------------------------------------
 // Q4_0 (kernels/q4_0.py:14-33), HBM-bound. A warp owns tiles of 32 consecutive
-// 32-blocks, read with fully coalesced 16-byte loads (lane l: bytes 16 l + 512 j of the
-// tile). The loads of the warp's next tile are issued before the current tile is
-// quantized, so memory stays busy while the warp computes. Tiles are parked in shared
-// memory and each lane quantizes one whole block from there: no shuffles, one
-// reciprocal per block. d = max / -8 is computed as max * -0.125 (the same IEEE value).
+// 32-blocks. Tiles stream into a per-warp ring of shared-memory stages with cp.async
+// (coalesced 16-byte copies, lane l: bytes 16 l + 512 j of the tile), STAGES - 1 tiles
+// ahead of the one being quantized, so memory stays busy without holding the data in
+// registers. Each lane then quantizes one whole block: no shuffles, one reciprocal per
+// block. d = max / -8 is computed as max * -0.125 (the same IEEE value).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
 template <int ES>  // source element size in bytes
-__global__ void __launch_bounds__(256) q4_0_kernel(QuantArgs a) {
-    constexpr int BB = 18, WARPS = 8, TILE = 32 * 32 * ES, NV = TILE / 512;
-    __shared__ __align__(16) uint8_t s_in[WARPS][TILE];
-    __shared__ __align__(16) uint8_t s_out[WARPS][32 * BB];
+__global__ void __launch_bounds__(256, 3) q4_0_kernel(QuantArgs a) {
+    constexpr int BB = 18, WARPS = 8, TILE = 32 * 32 * ES, NV = TILE / 512, STAGES = ES == 2 ? 4 : 3;
+    extern __shared__ __align__(16) uint8_t q40_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint8_t* si = s_in[warp];
-    uint8_t* so = s_out[warp];
+    uint8_t* ring = q40_smem + warp * (STAGES * TILE + 32 * BB);
+    uint8_t* so = ring + STAGES * TILE;
     const uint8_t* src = static_cast<const uint8_t*>(a.src);
     const int64_t ntile = (a.nblk + 31) / 32, lim = a.nblk * 32 * ES;
     const int64_t stride = (int64_t)gridDim.x * WARPS;
-    int64_t tile = (int64_t)blockIdx.x * WARPS + warp;
-    uint4 r[NV];
-    auto fetch = [&](int64_t t) {
+    const int64_t t_first = (int64_t)blockIdx.x * WARPS + warp;
+    auto issue = [&](int64_t t, int stage) {  // one commit group per tile, empty past the end
+        if (t < ntile) {
 #pragma unroll
-        for (int j = 0; j < NV; j++) {
-            const int64_t off = t * TILE + 512 * j + 16 * lane;
-            r[j] = (t < ntile && off < lim) ? __ldg(reinterpret_cast<const uint4*>(src + off)) : make_uint4(0, 0, 0, 0);
+            for (int j = 0; j < NV; j++) {
+                const int64_t off = t * TILE + 512 * j + 16 * lane;
+                cp_async16(ring + stage * TILE + 512 * j + 16 * lane, off < lim ? src + off : src, off < lim ? 16 : 0);
+            }
         }
+        cp_async_commit();
     };
-    fetch(tile);
-    for (; tile < ntile; tile += stride) {
 #pragma unroll
-        for (int j = 0; j < NV; j++) *reinterpret_cast<uint4*>(si + 512 * j + 16 * lane) = r[j];
-        __syncwarp();
-        fetch(tile + stride);
+    for (int st = 0; st < STAGES - 1; st++) issue(t_first + st * stride, st);
+    int stage = 0;
+    for (int64_t tile = t_first; tile < ntile; tile += stride) {
+        issue(tile + (STAGES - 1) * stride, (stage + STAGES - 1) % STAGES);
+        cp_async_wait<STAGES - 1>();  // this lane's copies of `tile` have landed
+        __syncwarp();                 // ... and every other lane's
         const int nvalid = (int)min((int64_t)32, a.nblk - tile * 32);
-        float x[32];
-        const uint8_t* blk = si + lane * 32 * ES;
+        float x[32], mx, mn;
+        const uint8_t* blk = ring + stage * TILE + lane * 32 * ES;
         if (ES == 4) {
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const float4 f = reinterpret_cast<const float4*>(blk)[i];
                 x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
             }
+            mx = x[0];
+            mn = x[0];
+#pragma unroll
+            for (int i = 1; i < 32; i++) { mx = fmaxf(mx, x[i]); mn = fminf(mn, x[i]); }
         } else {
+            // block max / min on packed pairs (exact for 16-bit floats), then widen
+            uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const uint4 t = reinterpret_cast<const uint4*>(blk)[i];
-                const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
+                w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
+            }
+            if (a.src_type == SRC_BF16) {
+                __nv_bfloat162 hx = *reinterpret_cast<const __nv_bfloat162*>(&w[0]), hn = hx;
 #pragma unroll
-                for (int h = 0; h < 4; h++) {
-                    const uint32_t lo = w4[h] & 0xFFFFu, hi = w4[h] >> 16;
-                    if (a.src_type == SRC_BF16) {
-                        x[8 * i + 2 * h] = __uint_as_float(lo << 16);
-                        x[8 * i + 2 * h + 1] = __uint_as_float(hi << 16);
-                    } else {
-                        x[8 * i + 2 * h] = __half2float(__ushort_as_half((unsigned short)lo));
-                        x[8 * i + 2 * h + 1] = __half2float(__ushort_as_half((unsigned short)hi));
-                    }
+                for (int i = 1; i < 16; i++) {
+                    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+                    hx = __hmax2(hx, v);
+                    hn = __hmin2(hn, v);
+                }
+                mx = fmaxf(__low2float(hx), __high2float(hx));
+                mn = fminf(__low2float(hn), __high2float(hn));
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    x[2 * i] = __uint_as_float(w[i] * 65536u);
+                    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+                }
+            } else {
+                __half2 hx = *reinterpret_cast<const __half2*>(&w[0]), hn = hx;
+#pragma unroll
+                for (int i = 1; i < 16; i++) {
+                    const __half2 v = *reinterpret_cast<const __half2*>(&w[i]);
+                    hx = __hmax2(hx, v);
+                    hn = __hmin2(hn, v);
+                }
+                mx = fmaxf(__low2float(hx), __high2float(hx));
+                mn = fminf(__low2float(hn), __high2float(hn));
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    x[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xFFFFu)));
+                    x[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
                 }
             }
         }
         // signed value of the first largest |x|: max and min of the block decide it
         // unless both +amax and -amax occur, then the first one in order wins
-        float mx = x[0], mn = x[0];
-#pragma unroll
-        for (int i = 1; i < 32; i++) { mx = fmaxf(mx, x[i]); mn = fminf(mn, x[i]); }
         float m = mx > -mn ? mx : mn;
         if (mx == -mn) {
             float am;
@@ -109,9 +142,14 @@ __global__ void __launch_bounds__(256) q4_0_kernel(QuantArgs a) {
         }
         __syncwarp();
         store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
-        __syncwarp();
+        __syncwarp();  // the stage and the output staging are free again
+        stage = (stage + 1) % STAGES;
     }
+    cp_async_wait<0>();
 }
+
+template <int ES>
+constexpr int q4_0_smem() { return 8 * ((ES == 2 ? 4 : 3) * 32 * 32 * ES + 32 * 18); }
 
 // ---------------------------------------------------------------------------
 // Q2_K / Q4_K / Q5_K (kernels/q2_k.py:25-81, q4_k.py:25-79, q5_k.py:25-82)
@@ -602,9 +640,9 @@ static void qx_steps(int nmax, float* c) {  // qx_common.py:20-23
 }
 
 template <typename K>
-static int grid_for(K kernel, int64_t tiles, const LaunchCtx& ctx) {
+static int grid_for(K kernel, int64_t tiles, const LaunchCtx& ctx, size_t smem = 0) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1) per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
     int64_t g = (int64_t)per_sm * ctx.num_sms;
     return (int)(tiles < g ? (tiles > 0 ? tiles : 1) : g);
 }
@@ -619,10 +657,12 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
         const int64_t ctas = (a.nblk + 255) / 256;  // 8 warps x tiles of 32 blocks
         if (a.src_type == SRC_F32) {
             auto k = q4_0_kernel<4>;
-            q4_0_kernel<4><<<grid_for(k, ctas, ctx), 256, 0, st>>>(a);
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q4_0_smem<4>());
+            q4_0_kernel<4><<<grid_for(k, ctas, ctx, q4_0_smem<4>()), 256, q4_0_smem<4>(), st>>>(a);
         } else {
             auto k = q4_0_kernel<2>;
-            q4_0_kernel<2><<<grid_for(k, ctas, ctx), 256, 0, st>>>(a);
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q4_0_smem<2>());
+            q4_0_kernel<2><<<grid_for(k, ctas, ctx, q4_0_smem<2>()), 256, q4_0_smem<2>(), st>>>(a);
         }
         break;
     }
