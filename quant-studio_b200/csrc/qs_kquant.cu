@@ -164,7 +164,7 @@ template <>
 struct QkxTraits<QS_Q5_K> { static constexpr int GS = 32, NMAX = 31, BB = 176, QPMAX = 63; static constexpr float SIGFAC = 2.0f; };
 
 template <int T, bool IMAT>
-__global__ void __launch_bounds__(256) qkx_kernel(QuantArgs a, KParams p) {
+__global__ void __launch_bounds__(256, 2) qkx_kernel(QuantArgs a, KParams p) {
     using Tr = QkxTraits<T>;
     constexpr int GS = Tr::GS, NG = QK_K / GS, SBT = 256 / NG, BB = Tr::BB;
     constexpr bool MAD = (T == QS_Q2_K) && !IMAT;
