@@ -14,7 +14,10 @@
 // The weighted distance of one candidate is a sum over positions of terms that depend
 // only on the position and the candidate's level there, so a lane first tabulates the
 // 4 x 8 (IQ2) or 8 x 4 (IQ3) terms of its search, computed exactly as the reference
-// does, and then needs one table read and one add per position and candidate.
+// does, and then needs one table read and one add per position and candidate. The
+// tables of all lanes of a CTA share one array of 256-byte rows at the start of shared
+// memory, column (warp * 32 + lane): a term's address is the candidate's level bits,
+// shifted into bits 8..11, OR-ed with the lane's byte column, plus a constant row.
 #include <algorithm>
 #include <vector>
 
@@ -29,8 +32,10 @@ namespace qs {
 // ---------------------------------------------------------------------------
 struct IqGridDev {
     const uint16_t* kgrid;  // grid index -> code
-    const uint32_t* nbr;    // code index -> 0x80000000 | grid index (on grid) or off << 9 | len
-    const uint32_t* list;   // neighbour lists, code << 16 | grid index, (distance, index) order
+    const uint32_t* nbr;    // code index -> 0x80000000 | code (on grid) or quad offset << 9 | quads
+    const uint16_t* list;   // neighbour lists as codes, (distance, index) order, padded to whole
+                            // quads with copies of the last code (a copy never wins a strict <)
+    const int16_t* kmap;    // code -> grid index (-1 off the grid)
     int grid;
 };
 
@@ -45,11 +50,12 @@ enum { G_IQ2XXS = 0, G_IQ2XS, G_IQ2S, G_IQ3XXS, G_IQ3S };
 // iq2.py:31-74, iq2xs_common.py:41-95, iq3_common.py:29-68). IQ2 codes are indexed in
 // base 3 because sweep levels are clamped to 0..2, IQ3 codes directly (levels 0..7).
 static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwant, std::vector<uint32_t>& nbr,
-                       std::vector<uint32_t>& list) {
+                       std::vector<uint16_t>& list, std::vector<int16_t>& kmap16) {
     const int mask = (1 << bits) - 1;
     const int kmap_size = bits == 2 ? 43692 : 4096;
     std::vector<int> kmap(kmap_size, -1);
     for (int i = 0; i < G; i++) kmap[kgrid[i]] = i;
+    kmap16.assign(kmap.begin(), kmap.end());
     const int nidx = bits == 2 ? 6561 : 4096;
     nbr.assign(nidx, 0);
     std::vector<int64_t> keys(G);
@@ -62,7 +68,7 @@ static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwa
             code = idx;
         }
         if (kmap[code] >= 0) {
-            nbr[idx] = 0x80000000u | (uint32_t)kmap[code];
+            nbr[idx] = 0x80000000u | (uint32_t)code;
             continue;
         }
         for (int i = 0; i < G; i++) {
@@ -83,11 +89,9 @@ static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwa
             if (ndist > nwant) break;
             n++;
         }
-        nbr[idx] = ((uint32_t)list.size() << 9) | (uint32_t)n;
-        for (int i = 0; i < n; i++) {
-            const int gi = (int)(keys[i] % 65536);
-            list.push_back(((uint32_t)kgrid[gi] << 16) | (uint32_t)gi);
-        }
+        const int nq = (n + 3) / 4;  // quads of 4 codes, one 8-byte load each
+        nbr[idx] = ((uint32_t)(list.size() / 4) << 9) | (uint32_t)nq;
+        for (int i = 0; i < 4 * nq; i++) list.push_back(kgrid[keys[i < n ? i : n - 1] % 65536]);
     }
 }
 
@@ -96,12 +100,13 @@ cudaError_t iq_tables_create(IqTables** out) {
         {KGRID_2BIT_256, 256, 2, 8, 2}, {KGRID_2BIT_512, 512, 2, 8, 2}, {KGRID_2BIT_1024, 1024, 2, 8, 1},
         {KGRID_3BIT_256, 256, 3, 4, 2}, {KGRID_3BIT_512, 512, 3, 4, 3}};
     std::vector<uint32_t> nbr[5];
-    std::vector<uint32_t> list[5];
+    std::vector<uint16_t> list[5];
+    std::vector<int16_t> kmap[5];
     size_t total = 0;
     auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
     for (int t = 0; t < 5; t++) {
-        build_grid(specs[t].grid, specs[t].G, specs[t].bits, specs[t].npos, specs[t].nwant, nbr[t], list[t]);
-        total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 4 + 16);
+        build_grid(specs[t].grid, specs[t].G, specs[t].bits, specs[t].npos, specs[t].nwant, nbr[t], list[t], kmap[t]);
+        total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 2 + 16) + al(kmap[t].size() * 2);
     }
     char* mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, total);
@@ -114,16 +119,19 @@ cudaError_t iq_tables_create(IqTables** out) {
         o += al(specs[t].G * 2);
         uint32_t* nb = reinterpret_cast<uint32_t*>(mem + o);
         o += al(nbr[t].size() * 4);
-        uint32_t* ls = reinterpret_cast<uint32_t*>(mem + o);
-        o += al(list[t].size() * 4 + 16);
+        uint16_t* ls = reinterpret_cast<uint16_t*>(mem + o);
+        o += al(list[t].size() * 2 + 16);
+        int16_t* km = reinterpret_cast<int16_t*>(mem + o);
+        o += al(kmap[t].size() * 2);
         if ((e = cudaMemcpy(kg, specs[t].grid, specs[t].G * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
             (e = cudaMemcpy(nb, nbr[t].data(), nbr[t].size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
-            (e = cudaMemcpy(ls, list[t].data(), list[t].size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            (e = cudaMemcpy(ls, list[t].data(), list[t].size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
+            (e = cudaMemcpy(km, kmap[t].data(), kmap[t].size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
             cudaFree(mem);
             delete T;
             return e;
         }
-        T->g[t] = IqGridDev{kg, nb, ls, specs[t].G};
+        T->g[t] = IqGridDev{kg, nb, ls, km, specs[t].G};
     }
     *out = T;
     return cudaSuccess;
@@ -182,31 +190,86 @@ struct IqParams {
 constexpr int IQ_WARPS = 2;      // warps per CTA; each warp owns 32 groups
 constexpr int IQ_CAP = 256;      // queued searches per warp
 constexpr int IQ_FINAL = 15;     // tag slot of the final reprojection
-constexpr int IQ_BINS = 293;     // list lengths 1..292 (the longest IQ2_XS list)
+constexpr int IQ_BINS = 74;      // list lengths in quads, 1..73 (the longest IQ2_XS list has 292 codes)
+constexpr uint32_t IQ_SEARCHED = 1u << 16;  // flag beside a resolved code: it came from a search
+
+// Rows of the CTA term table (256 bytes each: 64 columns of f32, warp * 32 + lane).
+// IQ2 (16-bit codes, 2 bits per position): rows 0..15 hold t0 + t1 for the pair of
+// levels (code & 15); positions 3, 5, 7 have a level stride of 4 rows and interleave
+// in rows 16..30; positions 2, 4, 6 have consecutive rows from 32, 36, 40.
+// IQ3 (12-bit codes, 3 bits per position): positions 3 and 1 take the even and odd rows
+// 0..15 (stride 2), positions 0 and 2 rows 16..23 and 24..31.
+template <int NPOS> struct IqRows;
+template <> struct IqRows<8> {
+    static constexpr int N = 44;
+    __host__ __device__ static constexpr int row(int j, int l) {
+        return j == 2 ? 32 + l : j == 3 ? 16 + 4 * l : j == 4 ? 36 + l : j == 5 ? 17 + 4 * l : j == 6 ? 40 + l : 18 + 4 * l;
+    }
+};
+template <> struct IqRows<4> {
+    static constexpr int N = 32;
+    __host__ __device__ static constexpr int row(int j, int l) {
+        return j == 0 ? 16 + l : j == 1 ? 1 + 2 * l : j == 2 ? 24 + l : 2 * l;
+    }
+};
 
 template <class Tr>
 struct IqWarpSmem {
     static constexpr int NB = IQ_CAP / (32 * Tr::NSUB);  // sweep steps per batch
-    static constexpr int NT = Tr::NPOS == 8 ? 16 + 6 * 4 : 32;  // IQ2: pair table of positions 0,1 + 6 x 4
-    float xv[32][Tr::GS + 1];    // search-space values of every group (|x|, parity-folded); +1: no bank clash
-    float wv[32][Tr::GS + 1];    // sqrt of the weights
-    float tbl[NT > 32 ? NT : 32][32];  // distance terms of each lane's search [entry][lane];
+    float xv[32][Tr::GS + 1];    // search-space values of every group (|x|, parity-folded); +1: no bank clash;
                                  // holds the superblock squares while the weights are computed
+    float wv[32][Tr::GS + 1];    // sqrt of the weights
     float psc[32][NB + 1];       // per group: search scale of each batch step, then the final scale
-    uint32_t off[IQ_CAP];
-    uint16_t len[IQ_CAP];
+    uint32_t off[IQ_CAP];        // list start, in quads
+    uint16_t len[IQ_CAP];        // list length, in quads
     uint16_t tag[IQ_CAP];        // group | slot << 5 | subgroup << 9
     uint16_t ord[IQ_CAP];        // searches in order of list length
     uint16_t rank[IQ_CAP];
     uint32_t hist[(IQ_BINS + 1) / 2];  // two 16-bit counters (then bin starts) per word
-    uint16_t win[32][NB][Tr::NSUB];  // resolved grid index (| 0x8000 when it came from a search)
+    uint32_t win[32][NB][Tr::NSUB];    // resolved code (| IQ_SEARCHED when it came from a search)
     float part[4][8];
     int nq;
 };
 
 template <class Tr>
+__host__ __device__ constexpr size_t iq_tbl_bytes() { return (size_t)IqRows<Tr::NPOS>::N * 256; }
+
+template <class Tr>
 constexpr size_t iq_smem_bytes() {
-    return IQ_WARPS * sizeof(IqWarpSmem<Tr>) + 64 * 4 + IQ_WARPS * 4 * Tr::BB + 64;
+    return iq_tbl_bytes<Tr>() + IQ_WARPS * sizeof(IqWarpSmem<Tr>) + 64 * 4 + IQ_WARPS * 4 * Tr::BB + 64;
+}
+
+// One distance term: constant row R plus the lane's column byte and the level bits.
+template <int R>
+__device__ __forceinline__ float iq_term(const unsigned char* tb, uint32_t a) {
+    return *reinterpret_cast<const float*>(tb + R * 256 + a);
+}
+
+// Weighted distance of the code in the low (HI = false) or high half of w; lb is the
+// lane's column byte. The terms are added in the reference's order, position 0 first.
+template <int NPOS, bool HI>
+__device__ __forceinline__ float iq_dist(const unsigned char* tb, uint32_t w, uint32_t lb) {
+    using R = IqRows<NPOS>;
+    if (NPOS == 8) {
+        const uint32_t a = HI ? w >> 8 : w << 8, b = HI ? w >> 12 : w << 4, c = HI ? w >> 16 : w,
+                       d = HI ? w >> 20 : w >> 4;
+        float s = iq_term<0>(tb, (a & 0xF00) | lb);
+        s = __fadd_rn(s, iq_term<R::row(2, 0)>(tb, (b & 0x300) | lb));
+        s = __fadd_rn(s, iq_term<R::row(3, 0)>(tb, (b & 0xC00) | lb));
+        s = __fadd_rn(s, iq_term<R::row(4, 0)>(tb, (c & 0x300) | lb));
+        s = __fadd_rn(s, iq_term<R::row(5, 0)>(tb, (c & 0xC00) | lb));
+        s = __fadd_rn(s, iq_term<R::row(6, 0)>(tb, (d & 0x300) | lb));
+        s = __fadd_rn(s, iq_term<R::row(7, 0)>(tb, (d & 0xC00) | lb));
+        return s;
+    } else {
+        const uint32_t a = HI ? w >> 8 : w << 8, b = HI ? w >> 10 : w << 6, c = HI ? w >> 14 : w << 2,
+                       d = HI ? w >> 16 : w;
+        float s = iq_term<R::row(0, 0)>(tb, (a & 0x700) | lb);
+        s = __fadd_rn(s, iq_term<R::row(1, 0)>(tb, (b & 0xE00) | lb));
+        s = __fadd_rn(s, iq_term<R::row(2, 0)>(tb, (c & 0x700) | lb));
+        s = __fadd_rn(s, iq_term<R::row(3, 0)>(tb, (d & 0xE00) | lb));
+        return s;
+    }
 }
 
 __device__ __forceinline__ int warp_excl_scan(int v, int lane, int& total) {
@@ -260,6 +323,10 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
     }
     __syncwarp();
 
+    extern __shared__ __align__(16) unsigned char smem[];
+    const unsigned char* tb = smem;
+    const uint32_t lb = (uint32_t)(threadIdx.x & (IQ_WARPS * 32 - 1)) * 4;  // this lane's column byte
+    using R = IqRows<Tr::NPOS>;
     for (int pb = 0; pb < P; pb += 32) {
         const int i = pb + lane;
         if (i < P) {
@@ -271,12 +338,10 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
             float sg[Tr::NLEV];
 #pragma unroll
             for (int l = 0; l < Tr::NLEV; l++) sg[l] = sc * (float)(2 * l + 1);
-            const uint32_t* lp = G.list + off;
-            float bd = 0.0f;
-            int bp = -1;
+            unsigned char* tw = smem + lb;
+            auto put = [&](int row, float t) { *reinterpret_cast<float*>(tw + row * 256) = t; };
+            // terms t_j(l) = (wv_j * (sc v_l - xv_j)) * (sc v_l - xv_j)
             if (Tr::NPOS == 8) {
-                // terms t_j(l) = (wv_j * (sc v_l - xv_j)) * (sc v_l - xv_j); the sum runs from
-                // position 0, so t_0 + t_1 is one table (16 entries), then 6 x 4 entries
                 float t0[4], t1[4];
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
@@ -287,13 +352,13 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
                         const float t = (wj * df) * df;
                         if (j == 0) t0[l] = t;
                         else if (j == 1) t1[l] = t;
-                        else W.tbl[16 + (j - 2) * 4 + l][lane] = t;
+                        else put(R::row(j, l), t);
                     }
                 }
 #pragma unroll
                 for (int l1 = 0; l1 < 4; l1++)
 #pragma unroll
-                    for (int l0 = 0; l0 < 4; l0++) W.tbl[l0 + 4 * l1][lane] = t0[l0] + t1[l1];
+                    for (int l0 = 0; l0 < 4; l0++) put(l0 + 4 * l1, t0[l0] + t1[l1]);
             } else {
 #pragma unroll
                 for (int j = 0; j < Tr::NPOS; j++) {
@@ -301,39 +366,29 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
 #pragma unroll
                     for (int l = 0; l < Tr::NLEV; l++) {
                         const float df = sg[l] - xj;
-                        W.tbl[j * Tr::NLEV + l][lane] = (wj * df) * df;
+                        put(R::row(j, l), (wj * df) * df);
                     }
                 }
             }
-            auto dist = [&](int code) -> float {
-                if (Tr::NPOS == 8) {
-                    float d2 = W.tbl[code & 15][lane];
-#pragma unroll
-                    for (int j = 2; j < 8; j++) d2 = __fadd_rn(d2, W.tbl[16 + (j - 2) * 4 + ((code >> (2 * j)) & 3)][lane]);
-                    return d2;
-                } else {
-                    float d2 = W.tbl[code & 7][lane];
-#pragma unroll
-                    for (int j = 1; j < 4; j++) d2 = __fadd_rn(d2, W.tbl[j * 8 + ((code >> (3 * j)) & 7)][lane]);
-                    return d2;
-                }
+            // first candidate, then strict < over the rest: the first of equal distances wins
+            const uint2* lp = reinterpret_cast<const uint2*>(G.list) + off;
+            uint2 v = __ldg(lp);
+            float bd = iq_dist<Tr::NPOS, false>(tb, v.x, lb);
+            uint32_t bc = v.x & 0xFFFF;
+            auto take = [&](float d2, uint32_t code) {
+                if (d2 < bd) { bd = d2; bc = code; }
             };
-            int c = 0;
-            for (; c + 4 <= n; c += 4) {
-                uint32_t e[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) e[u] = __ldg(lp + c + u);
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float d2 = dist((int)(e[u] >> 16));
-                    if (bp < 0 || d2 < bd) { bd = d2; bp = c + u; }
-                }
+            take(iq_dist<Tr::NPOS, true>(tb, v.x, lb), v.x >> 16);
+            take(iq_dist<Tr::NPOS, false>(tb, v.y, lb), v.y & 0xFFFF);
+            take(iq_dist<Tr::NPOS, true>(tb, v.y, lb), v.y >> 16);
+            for (int c = 1; c < n; c++) {
+                v = __ldg(lp + c);
+                take(iq_dist<Tr::NPOS, false>(tb, v.x, lb), v.x & 0xFFFF);
+                take(iq_dist<Tr::NPOS, true>(tb, v.x, lb), v.x >> 16);
+                take(iq_dist<Tr::NPOS, false>(tb, v.y, lb), v.y & 0xFFFF);
+                take(iq_dist<Tr::NPOS, true>(tb, v.y, lb), v.y >> 16);
             }
-            for (; c < n; c++) {
-                const float d2 = dist((int)(__ldg(lp + c) >> 16));
-                if (bp < 0 || d2 < bd) { bd = d2; bp = c; }
-            }
-            W.win[g][slot == IQ_FINAL ? 0 : slot][q] = (uint16_t)((__ldg(lp + bp) & 0xFFFF) | 0x8000);
+            W.win[g][slot == IQ_FINAL ? 0 : slot][q] = bc | IQ_SEARCHED;
         }
     }
     __syncwarp();
@@ -371,12 +426,12 @@ __device__ __forceinline__ void iq_enqueue(IqWarpSmem<Tr>& W, int lane, int nmin
     __syncwarp();
 }
 
-// grid values (2l+1) of the winners of one group -> q[GS]
+// grid values (2l+1) of the resolved codes of one group -> q[GS]
 template <class Tr>
-__device__ __forceinline__ void iq_decode(const uint16_t* kgrid, const uint16_t* win, float* q) {
+__device__ __forceinline__ void iq_decode(const uint32_t* win, float* q) {
 #pragma unroll
     for (int s = 0; s < Tr::NSUB; s++) {
-        const int code = __ldg(kgrid + (win[s] & 0x7FFF));
+        const int code = (int)(win[s] & 0xFFFF);
 #pragma unroll
         for (int j = 0; j < Tr::NPOS; j++) q[s * Tr::NPOS + j] = (float)(2 * ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1)) + 1);
     }
@@ -406,8 +461,8 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
     constexpr int GS = Tr::GS, NSUB = Tr::NSUB, SBG = QK_K / GS, SBW = 32 / SBG, SBT = IQ_WARPS * SBW, BB = Tr::BB;
     constexpr int NB = WS::NB;
     extern __shared__ __align__(16) unsigned char smem[];
-    WS* wsm = reinterpret_cast<WS*>(smem);
-    float* s_c = reinterpret_cast<float*>(smem + IQ_WARPS * sizeof(WS));
+    WS* wsm = reinterpret_cast<WS*>(smem + iq_tbl_bytes<Tr>());  // the term table comes first
+    float* s_c = reinterpret_cast<float*>(smem + iq_tbl_bytes<Tr>() + IQ_WARPS * sizeof(WS));
     float* s_qp = s_c + 32;
     uint8_t* s_out = reinterpret_cast<uint8_t*>(s_qp + 32);
 
@@ -426,7 +481,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
 
         // weights (iq2.py:429-431, iq2_xs.py:27-29, iq2_s.py:28-30, iq3_xxs.py:40-45)
         if (IMAT) {
-            float* sq = &W.tbl[0][0] + sbl * QK_K;
+            float* sq = &W.xv[0][0] + sbl * QK_K;  // xv is written only after the weights
 #pragma unroll
             for (int i = 0; i < GS; i++) sq[gl * GS + i] = x[i] * x[i];
             __syncwarp();
@@ -494,9 +549,10 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             else scale = __fdiv_rn(gmax, 15.0f);
         }
         float best = 0.0f;
-        uint16_t cur[NSUB];
+        uint32_t cur[NSUB];
+        const uint32_t cur0 = Tr::RP == RP_ALL_REDO ? (uint32_t)__ldg(G.kgrid) | IQ_SEARCHED : (uint32_t)__ldg(G.kgrid);
 #pragma unroll
-        for (int s = 0; s < NSUB; s++) cur[s] = Tr::RP == RP_ALL_REDO ? 0x8000 : 0;  // og_init: IQ3_S starts off-grid
+        for (int s = 0; s < NSUB; s++) cur[s] = cur0;  // grid index 0; og_init: IQ3_S starts off-grid
         __syncwarp();
 
         // sweep over the candidate scales, NB steps per batch of searches
@@ -511,14 +567,14 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
                 for (int q = 0; q < NSUB; q++) {
                     uint32_t v;
                     if (iq_code<Tr>(xval, q, inv, G, v)) { vs[nm] = v; qs[nm] = q; nm++; }
-                    else W.win[lane][j][q] = (uint16_t)(v & 0x7FFF);
+                    else W.win[lane][j][q] = v & 0xFFFF;
                 }
                 iq_enqueue<Tr>(W, lane, nm, vs, qs, j);
             }
             iq_flush<Tr>(W, G, lane);
             for (int j = 0; j < nb; j++) {
                 float qv[GS], sumqx, sumq2;
-                iq_decode<Tr>(G.kgrid, W.win[lane][j], qv);
+                iq_decode<Tr>(W.win[lane][j], qv);
                 iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
                 if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
                     const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
@@ -534,7 +590,7 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
         // final reprojection at the accepted scale + least-squares refit
         bool anyoff = false, allon = true;
 #pragma unroll
-        for (int q = 0; q < NSUB; q++) { anyoff |= (cur[q] & 0x8000) != 0; allon &= (cur[q] & 0x8000) == 0; }
+        for (int q = 0; q < NSUB; q++) { anyoff |= (cur[q] & IQ_SEARCHED) != 0; allon &= (cur[q] & IQ_SEARCHED) == 0; }
         bool redo;
         float inv;
         if (Tr::RP == RP_ALL_PROJ) {
@@ -553,31 +609,33 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             int qs[NSUB], nm = 0;
 #pragma unroll
             for (int q = 0; q < NSUB; q++) {
-                const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & 0x8000));
+                const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & IQ_SEARCHED));
                 W.win[lane][0][q] = cur[q];
                 if (want) {
                     uint32_t v;
                     if (iq_code<Tr>(xval, q, inv, G, v)) { vs[nm] = v; qs[nm] = q; nm++; }
-                    else W.win[lane][0][q] = (uint16_t)(v & 0x7FFF);
+                    else W.win[lane][0][q] = v & 0xFFFF;
                 }
             }
             __syncwarp();
             iq_enqueue<Tr>(W, lane, nm, vs, qs, IQ_FINAL);
         }
         iq_flush<Tr>(W, G, lane);
-        uint16_t fin[NSUB];
+        uint32_t fin[NSUB];
 #pragma unroll
-        for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][0][q] & 0x7FFF;
+        for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][0][q] & 0xFFFF;
         {
             float qv[GS], sumqx, sumq2;
-            iq_decode<Tr>(G.kgrid, fin, qv);
+            iq_decode<Tr>(fin, qv);
             iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
             if (redo && sumq2 > 0.0f) scale = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
         }
         if (!redo) {
 #pragma unroll
-            for (int q = 0; q < NSUB; q++) fin[q] = cur[q] & 0x7FFF;
+            for (int q = 0; q < NSUB; q++) fin[q] = cur[q] & 0xFFFF;
         }
+#pragma unroll
+        for (int q = 0; q < NSUB; q++) fin[q] = (uint32_t)__ldg(G.kmap + fin[q]);  // code -> grid index
         // negative least-squares scale: flip the scale and all the signs
         if (active && scale < 0.0f) {
             scale = -scale;
