@@ -106,6 +106,7 @@ cudaError_t iq_tables_create(IqTables** out) {
     auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
     for (int t = 0; t < 5; t++) {
         build_grid(specs[t].grid, specs[t].G, specs[t].bits, specs[t].npos, specs[t].nwant, nbr[t], list[t], kmap[t]);
+        if (list[t].size() / 4 > 65535) return cudaErrorInvalidValue;  // queue entries hold 16-bit quad offsets
         total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 2 + 16) + al(kmap[t].size() * 2);
     }
     char* mem = nullptr;
@@ -189,6 +190,7 @@ struct IqParams {
 
 constexpr int IQ_WARPS = 2;      // warps per CTA; each warp owns 32 groups
 constexpr int IQ_CAP = 256;      // queued searches per warp
+constexpr int IQ_MIN_CTAS = 6;   // resident CTAs per SM the register budget is sized for (12 warps)
 constexpr int IQ_FINAL = 15;     // tag slot of the final reprojection
 constexpr int IQ_BINS = 74;      // list lengths in quads, 1..73 (the longest IQ2_XS list has 292 codes)
 constexpr uint32_t IQ_SEARCHED = 1u << 16;  // flag beside a resolved code: it came from a search
@@ -216,17 +218,20 @@ template <> struct IqRows<4> {
 template <class Tr>
 struct IqWarpSmem {
     static constexpr int NB = IQ_CAP / (32 * Tr::NSUB);  // sweep steps per batch
-    float xv[32][Tr::GS + 1];    // search-space values of every group (|x|, parity-folded); +1: no bank clash;
-                                 // holds the superblock squares while the weights are computed
-    float wv[32][Tr::GS + 1];    // sqrt of the weights
+    static constexpr int XS = Tr::GS + 4;  // row pitch: 16-byte rows, and 8 lanes' float4s hit 8 distinct bank quads
+    static constexpr int WINS = NB * Tr::NSUB + 1;  // odd word pitch: lane-indexed accesses are conflict-free
+    __align__(16) float xv[32][XS];  // search-space values of every group (|x|, parity-folded);
+                                     // holds the superblock squares while the weights are computed
+    __align__(16) float wv[32][XS];  // sqrt of the weights
     float psc[32][NB + 1];       // per group: search scale of each batch step, then the final scale
-    uint32_t off[IQ_CAP];        // list start, in quads
-    uint16_t len[IQ_CAP];        // list length, in quads
+    uint16_t off[IQ_CAP];        // list start, in quads (every list table has fewer than 65536 quads)
     uint16_t tag[IQ_CAP];        // group | slot << 5 | subgroup << 9
-    uint16_t ord[IQ_CAP];        // searches in order of list length
-    uint16_t rank[IQ_CAP];
+    uint8_t len[IQ_CAP];         // list length, in quads
+    uint8_t ord[IQ_CAP];         // searches in order of list length
+    uint8_t rank[IQ_CAP];
     uint32_t hist[(IQ_BINS + 1) / 2];  // two 16-bit counters (then bin starts) per word
-    uint32_t win[32][NB][Tr::NSUB];    // resolved code (| IQ_SEARCHED when it came from a search)
+    uint32_t win[32][WINS];      // per step j and subgroup q, at j * NSUB + q: the resolved code
+                                 // (| IQ_SEARCHED when it came from a search)
     float part[4][8];
     int nq;
 };
@@ -295,7 +300,7 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
     for (int i = lane; i < P; i += 32) {
         const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i]);
         const int sh = 16 * (bin & 1);
-        W.rank[i] = (uint16_t)((atomicAdd(&W.hist[bin >> 1], 1u << sh) >> sh) & 0xFFFF);
+        W.rank[i] = (uint8_t)((atomicAdd(&W.hist[bin >> 1], 1u << sh) >> sh) & 0xFFFF);
     }
     __syncwarp();
     {
@@ -319,7 +324,7 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
     __syncwarp();
     for (int i = lane; i < P; i += 32) {
         const int bin = IQ_BINS - 1 - min(IQ_BINS - 1, (int)W.len[i]);
-        W.ord[((W.hist[bin >> 1] >> (16 * (bin & 1))) & 0xFFFF) + W.rank[i]] = (uint16_t)i;
+        W.ord[((W.hist[bin >> 1] >> (16 * (bin & 1))) & 0xFFFF) + W.rank[i]] = (uint8_t)i;
     }
     __syncwarp();
 
@@ -338,14 +343,25 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
             float sg[Tr::NLEV];
 #pragma unroll
             for (int l = 0; l < Tr::NLEV; l++) sg[l] = sc * (float)(2 * l + 1);
+            // the list's first quad is in flight while the terms are tabulated
+            const uint2* lp = reinterpret_cast<const uint2*>(G.list) + off;
+            const uint2 v0 = __ldg(lp);
             unsigned char* tw = smem + lb;
             auto put = [&](int row, float t) { *reinterpret_cast<float*>(tw + row * 256) = t; };
             // terms t_j(l) = (wv_j * (sc v_l - xv_j)) * (sc v_l - xv_j)
+            float xs[Tr::NPOS], ws[Tr::NPOS];
+#pragma unroll
+            for (int j = 0; j < Tr::NPOS; j += 4) {
+                const float4 xa = *reinterpret_cast<const float4*>(&W.xv[g][q * Tr::NPOS + j]);
+                const float4 wa = *reinterpret_cast<const float4*>(&W.wv[g][q * Tr::NPOS + j]);
+                xs[j] = xa.x; xs[j + 1] = xa.y; xs[j + 2] = xa.z; xs[j + 3] = xa.w;
+                ws[j] = wa.x; ws[j + 1] = wa.y; ws[j + 2] = wa.z; ws[j + 3] = wa.w;
+            }
             if (Tr::NPOS == 8) {
                 float t0[4], t1[4];
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    const float xj = W.xv[g][q * 8 + j], wj = W.wv[g][q * 8 + j];
+                    const float xj = xs[j], wj = ws[j];
 #pragma unroll
                     for (int l = 0; l < 4; l++) {
                         const float df = sg[l] - xj;
@@ -362,7 +378,7 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
             } else {
 #pragma unroll
                 for (int j = 0; j < Tr::NPOS; j++) {
-                    const float xj = W.xv[g][q * Tr::NPOS + j], wj = W.wv[g][q * Tr::NPOS + j];
+                    const float xj = xs[j], wj = ws[j];
 #pragma unroll
                     for (int l = 0; l < Tr::NLEV; l++) {
                         const float df = sg[l] - xj;
@@ -371,24 +387,22 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
                 }
             }
             // first candidate, then strict < over the rest: the first of equal distances wins
-            const uint2* lp = reinterpret_cast<const uint2*>(G.list) + off;
-            uint2 v = __ldg(lp);
-            float bd = iq_dist<Tr::NPOS, false>(tb, v.x, lb);
-            uint32_t bc = v.x & 0xFFFF;
+            float bd = iq_dist<Tr::NPOS, false>(tb, v0.x, lb);
+            uint32_t bc = v0.x & 0xFFFF;
             auto take = [&](float d2, uint32_t code) {
                 if (d2 < bd) { bd = d2; bc = code; }
             };
-            take(iq_dist<Tr::NPOS, true>(tb, v.x, lb), v.x >> 16);
-            take(iq_dist<Tr::NPOS, false>(tb, v.y, lb), v.y & 0xFFFF);
-            take(iq_dist<Tr::NPOS, true>(tb, v.y, lb), v.y >> 16);
-            for (int c = 1; c < n; c++) {
-                v = __ldg(lp + c);
+            auto quad = [&](const uint2 v) {
                 take(iq_dist<Tr::NPOS, false>(tb, v.x, lb), v.x & 0xFFFF);
                 take(iq_dist<Tr::NPOS, true>(tb, v.x, lb), v.x >> 16);
                 take(iq_dist<Tr::NPOS, false>(tb, v.y, lb), v.y & 0xFFFF);
                 take(iq_dist<Tr::NPOS, true>(tb, v.y, lb), v.y >> 16);
-            }
-            W.win[g][slot == IQ_FINAL ? 0 : slot][q] = bc | IQ_SEARCHED;
+            };
+            take(iq_dist<Tr::NPOS, true>(tb, v0.x, lb), v0.x >> 16);
+            take(iq_dist<Tr::NPOS, false>(tb, v0.y, lb), v0.y & 0xFFFF);
+            take(iq_dist<Tr::NPOS, true>(tb, v0.y, lb), v0.y >> 16);
+            for (int c = 1; c < n; c++) quad(__ldg(lp + c));
+            W.win[g][(slot == IQ_FINAL ? 0 : slot) * Tr::NSUB + q] = bc | IQ_SEARCHED;
         }
     }
     __syncwarp();
@@ -396,10 +410,10 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
     __syncwarp();
 }
 
-// Tentative code of subgroup q at inverse scale inv; on-grid codes resolve at once
-// (writes win), off-grid ones are queued. Returns 1 if queued.
+// Index of the tentative code of subgroup q at inverse scale inv into the nbr table
+// (base 3 for IQ2: sweep levels are clamped to 0..2; the code itself for IQ3).
 template <class Tr>
-__device__ __forceinline__ int iq_code(const float* xval, int q, float inv, const IqGridDev& G, uint32_t& v) {
+__device__ __forceinline__ int iq_index(const float* xval, int q, float inv) {
     int idx = 0, mul = 1;
 #pragma unroll
     for (int j = 0; j < Tr::NPOS; j++) {
@@ -407,19 +421,22 @@ __device__ __forceinline__ int iq_code(const float* xval, int q, float inv, cons
         if (Tr::BITS == 2) { idx += l * mul; mul *= 3; }
         else idx |= l << (3 * j);
     }
-    v = __ldg(G.nbr + idx);
-    return (v >> 31) ? 0 : 1;
+    return idx;
 }
 
+// Queue the off-grid subgroups of this lane's group (bit q of `mask` set: nbr entry v[q]).
 template <class Tr>
-__device__ __forceinline__ void iq_enqueue(IqWarpSmem<Tr>& W, int lane, int nmine, const uint32_t* vs, const int* qs,
-                                           int slot) {
+__device__ __forceinline__ void iq_enqueue(IqWarpSmem<Tr>& W, int lane, uint32_t mask, const uint32_t* v, int slot) {
     int tot;
-    const int base = W.nq + warp_excl_scan(nmine, lane, tot);
-    for (int i = 0; i < nmine; i++) {
-        W.off[base + i] = vs[i] >> 9;
-        W.len[base + i] = (uint16_t)(vs[i] & 511);
-        W.tag[base + i] = (uint16_t)(lane | (slot << 5) | (qs[i] << 9));
+    int k = W.nq + warp_excl_scan(__popc(mask), lane, tot);
+#pragma unroll
+    for (int q = 0; q < Tr::NSUB; q++) {
+        if (mask & (1u << q)) {
+            W.off[k] = (uint16_t)(v[q] >> 9);
+            W.len[k] = (uint8_t)(v[q] & 511);
+            W.tag[k] = (uint16_t)(lane | (slot << 5) | (q << 9));
+            k++;
+        }
     }
     __syncwarp();
     if (lane == 0) W.nq += tot;
@@ -455,7 +472,7 @@ __device__ __forceinline__ void iq_sums(const float* w, const float* xval, const
 }
 
 template <int TYPE, bool IMAT>
-__global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDev G, IqParams prm) {
+__global__ void __launch_bounds__(IQ_WARPS * 32, IQ_MIN_CTAS) iq_kernel(QuantArgs a, IqGridDev G, IqParams prm) {
     using Tr = IqT<TYPE>;
     using WS = IqWarpSmem<Tr>;
     constexpr int GS = Tr::GS, NSUB = Tr::NSUB, SBG = QK_K / GS, SBW = 32 / SBG, SBT = IQ_WARPS * SBW, BB = Tr::BB;
@@ -528,9 +545,10 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
             }
         }
 #pragma unroll
-        for (int i = 0; i < GS; i++) {
-            W.xv[lane][i] = xval[i];
-            W.wv[lane][i] = sqrtf(w[i]);
+        for (int i = 0; i < GS; i += 4) {
+            *reinterpret_cast<float4*>(&W.xv[lane][i]) = make_float4(xval[i], xval[i + 1], xval[i + 2], xval[i + 3]);
+            *reinterpret_cast<float4*>(&W.wv[lane][i]) =
+                make_float4(sqrtf(w[i]), sqrtf(w[i + 1]), sqrtf(w[i + 2]), sqrtf(w[i + 3]));
         }
 
         const float gmax = max_of<GS>(xval);
@@ -558,30 +576,41 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
         // sweep over the candidate scales, NB steps per batch of searches
         for (int s0 = 0; s0 < Tr::NSTEP; s0 += NB) {
             const int nb = min(NB, Tr::NSTEP - s0);
-            for (int j = 0; j < nb; j++) {
-                const float inv = r * s_c[s0 + j];
-                W.psc[lane][j] = rcp_rn(inv);
-                uint32_t vs[NSUB];
-                int qs[NSUB], nm = 0;
+            // all codes of the batch first, so their table loads are in flight together
+            uint32_t nv[NB][NSUB];
 #pragma unroll
-                for (int q = 0; q < NSUB; q++) {
-                    uint32_t v;
-                    if (iq_code<Tr>(xval, q, inv, G, v)) { vs[nm] = v; qs[nm] = q; nm++; }
-                    else W.win[lane][j][q] = v & 0xFFFF;
+            for (int j = 0; j < NB; j++) {
+                if (j < nb) {
+                    const float inv = r * s_c[s0 + j];
+                    W.psc[lane][j] = rcp_rn(inv);
+#pragma unroll
+                    for (int q = 0; q < NSUB; q++) nv[j][q] = __ldg(G.nbr + iq_index<Tr>(xval, q, inv));
                 }
-                iq_enqueue<Tr>(W, lane, nm, vs, qs, j);
+            }
+#pragma unroll
+            for (int j = 0; j < NB; j++) {
+                if (j < nb) {
+                    uint32_t mask = 0;
+#pragma unroll
+                    for (int q = 0; q < NSUB; q++) {
+                        const uint32_t v = nv[j][q];
+                        if (v >> 31) W.win[lane][j * NSUB + q] = v & 0xFFFF;
+                        else mask |= 1u << q;
+                    }
+                    iq_enqueue<Tr>(W, lane, mask, nv[j], j);
+                }
             }
             iq_flush<Tr>(W, G, lane);
             for (int j = 0; j < nb; j++) {
                 float qv[GS], sumqx, sumq2;
-                iq_decode<Tr>(W.win[lane][j], qv);
+                iq_decode<Tr>(&W.win[lane][j * NSUB], qv);
                 iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
                 if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
                     const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
                     scale = ns;
                     best = ns * sumqx;
 #pragma unroll
-                    for (int q = 0; q < NSUB; q++) cur[q] = W.win[lane][j][q];
+                    for (int q = 0; q < NSUB; q++) cur[q] = W.win[lane][j * NSUB + q];
                 }
             }
             __syncwarp();
@@ -605,25 +634,25 @@ __global__ void __launch_bounds__(IQ_WARPS * 32) iq_kernel(QuantArgs a, IqGridDe
         }
         W.psc[lane][NB] = scale;
         {
-            uint32_t vs[NSUB];
-            int qs[NSUB], nm = 0;
+            uint32_t v[NSUB], mask = 0;
 #pragma unroll
             for (int q = 0; q < NSUB; q++) {
                 const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & IQ_SEARCHED));
-                W.win[lane][0][q] = cur[q];
-                if (want) {
-                    uint32_t v;
-                    if (iq_code<Tr>(xval, q, inv, G, v)) { vs[nm] = v; qs[nm] = q; nm++; }
-                    else W.win[lane][0][q] = v & 0xFFFF;
-                }
+                // not reprojected: keep the current code (read back below without its flag)
+                v[q] = want ? __ldg(G.nbr + iq_index<Tr>(xval, q, inv)) : 0x80000000u | cur[q];
+            }
+#pragma unroll
+            for (int q = 0; q < NSUB; q++) {
+                if (v[q] >> 31) W.win[lane][q] = v[q] & 0xFFFF;
+                else mask |= 1u << q;
             }
             __syncwarp();
-            iq_enqueue<Tr>(W, lane, nm, vs, qs, IQ_FINAL);
+            iq_enqueue<Tr>(W, lane, mask, v, IQ_FINAL);
         }
         iq_flush<Tr>(W, G, lane);
         uint32_t fin[NSUB];
 #pragma unroll
-        for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][0][q] & 0xFFFF;
+        for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][q] & 0xFFFF;
         {
             float qv[GS], sumqx, sumq2;
             iq_decode<Tr>(fin, qv);
