@@ -1,7 +1,7 @@
 // K-quant (Q2_K..Q6_K), IQ4_XS and Q4_0 kernels for sm_100a.
 //
 // Layout: one thread per quantization group (16 or 32 values in registers), the
-// threads of a superblock are consecutive lanes of one warp, a CTA of 256 threads
+// threads of a superblock are consecutive lanes of one warp, a CTA of 128 or 256 threads
 // works on a tile of 16 or 32 superblocks and stages the packed tile in shared
 // memory before a coalesced store. Reference for every formula: the eager torch path
 // of ngxson/quant-studio kernels/<type>.py (citations per kernel).
@@ -157,16 +157,16 @@ constexpr int q4_0_smem() { return 8 * ((ES == 2 ? 4 : 3) * 32 * 32 * ES + 32 * 
 template <int T>
 struct QkxTraits;
 template <>
-struct QkxTraits<QS_Q2_K> { static constexpr int GS = 16, NMAX = 3, BB = 84, QPMAX = 15; static constexpr float SIGFAC = 1.0f; };
+struct QkxTraits<QS_Q2_K> { static constexpr int GS = 16, NMAX = 3, BB = 84, QPMAX = 15, THREADS = 256, MIN_CTAS = 2; static constexpr float SIGFAC = 1.0f; };
 template <>
-struct QkxTraits<QS_Q4_K> { static constexpr int GS = 32, NMAX = 15, BB = 144, QPMAX = 63; static constexpr float SIGFAC = 2.0f; };
+struct QkxTraits<QS_Q4_K> { static constexpr int GS = 32, NMAX = 15, BB = 144, QPMAX = 63, THREADS = 128, MIN_CTAS = 3; static constexpr float SIGFAC = 2.0f; };
 template <>
-struct QkxTraits<QS_Q5_K> { static constexpr int GS = 32, NMAX = 31, BB = 176, QPMAX = 63; static constexpr float SIGFAC = 2.0f; };
+struct QkxTraits<QS_Q5_K> { static constexpr int GS = 32, NMAX = 31, BB = 176, QPMAX = 63, THREADS = 128, MIN_CTAS = 3; static constexpr float SIGFAC = 2.0f; };
 
 template <int T, bool IMAT>
-__global__ void __launch_bounds__(256, 2) qkx_kernel(QuantArgs a, KParams p) {
+__global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS) qkx_kernel(QuantArgs a, KParams p) {
     using Tr = QkxTraits<T>;
-    constexpr int GS = Tr::GS, NG = QK_K / GS, SBT = 256 / NG, BB = Tr::BB;
+    constexpr int GS = Tr::GS, NG = QK_K / GS, SBT = Tr::THREADS / NG, BB = Tr::BB;
     constexpr bool MAD = (T == QS_Q2_K) && !IMAT;
     __shared__ float s_steps[40], s_qp[8];
     __shared__ __align__(16) float s_sq[SBT * QK_K];  // squares, then the SB's level bytes
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(256, 2) qkx_kernel(QuantArgs a, KParams p) {
             }
         }
         __syncthreads();
-        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, 256);
+        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, Tr::THREADS);
         __syncthreads();
     }
 }
@@ -512,9 +512,11 @@ __device__ __forceinline__ int iq4nl_index(const float* kv, float al) {
     return (al - kv[mu - 1] < kv[mu] - al) ? mu - 1 : mu;
 }
 
+constexpr int IQ4XS_THREADS = 128, IQ4XS_MIN_CTAS = 3;  // 3 CTAs of 4 warps per SM at <= 168 registers
+
 template <bool IMAT>
-__global__ void __launch_bounds__(256) iq4xs_kernel(QuantArgs a) {
-    constexpr int GS = 32, NG = 8, SBT = 32, BB = 136;
+__global__ void __launch_bounds__(IQ4XS_THREADS, IQ4XS_MIN_CTAS) iq4xs_kernel(QuantArgs a) {
+    constexpr int GS = 32, NG = 8, SBT = IQ4XS_THREADS / NG, BB = 136;
     __shared__ float s_kv[16];
     __shared__ __align__(16) float s_sq[SBT * QK_K];
     __shared__ float s_part[SBT][8], s_sc[SBT][NG];
@@ -617,7 +619,7 @@ __global__ void __launch_bounds__(256) iq4xs_kernel(QuantArgs a) {
             for (int j = 0; j < 4; j++) o[4 + j] = (uint8_t)((lsq[2 * j] & 0xF) | ((lsq[2 * j + 1] & 0xF) << 4));
         }
         __syncthreads();
-        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, 256);
+        store_tile(a, s_out, tile * SBT, (int)min((int64_t)SBT, a.nblk - tile * SBT), BB, tid, IQ4XS_THREADS);
         __syncthreads();
     }
 }
@@ -640,9 +642,9 @@ static void qx_steps(int nmax, float* c) {  // qx_common.py:20-23
 }
 
 template <typename K>
-static int grid_for(K kernel, int64_t tiles, const LaunchCtx& ctx, size_t smem = 0) {
+static int grid_for(K kernel, int64_t tiles, const LaunchCtx& ctx, size_t smem = 0, int threads = 256) {
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm < 1) per_sm = 1;
     int64_t g = (int64_t)per_sm * ctx.num_sms;
     return (int)(tiles < g ? (tiles > 0 ? tiles : 1) : g);
 }
@@ -674,12 +676,12 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
         else if (type == QS_Q4_K) qkx_steps(-1.0f, 0.1f, 20, 15, p);
         else qkx_steps(-0.5f, 0.1f, 15, nmax, p);
         qp_steps(type == QS_Q2_K ? 15 : 63, p);
-        const int sbt = type == QS_Q2_K ? 16 : 32;
-        const int64_t tiles = (a.nblk + sbt - 1) / sbt;
 #define QS_LAUNCH_QKX(T, I)                                            \
     {                                                                  \
+        constexpr int NT = QkxTraits<T>::THREADS, SBT = NT / (QK_K / QkxTraits<T>::GS); \
         auto k = qkx_kernel<T, I>;                                     \
-        qkx_kernel<T, I><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a, p); \
+        const int64_t tiles = (a.nblk + SBT - 1) / SBT;                \
+        qkx_kernel<T, I><<<grid_for(k, tiles, ctx, 0, NT), NT, 0, st>>>(a, p); \
     }
         if (type == QS_Q4_K) { if (imat) QS_LAUNCH_QKX(QS_Q4_K, true) else QS_LAUNCH_QKX(QS_Q4_K, false) }
         else if (type == QS_Q5_K) { if (imat) QS_LAUNCH_QKX(QS_Q5_K, true) else QS_LAUNCH_QKX(QS_Q5_K, false) }
@@ -703,9 +705,10 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
         break;
     }
     case QS_IQ4_XS: {
-        const int64_t tiles = (a.nblk + 31) / 32;
-        if (imat) { auto k = iq4xs_kernel<true>; iq4xs_kernel<true><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a); }
-        else { auto k = iq4xs_kernel<false>; iq4xs_kernel<false><<<grid_for(k, tiles, ctx), 256, 0, st>>>(a); }
+        constexpr int SBT = IQ4XS_THREADS / 8;
+        const int64_t tiles = (a.nblk + SBT - 1) / SBT;
+        if (imat) { auto k = iq4xs_kernel<true>; iq4xs_kernel<true><<<grid_for(k, tiles, ctx, 0, IQ4XS_THREADS), IQ4XS_THREADS, 0, st>>>(a); }
+        else { auto k = iq4xs_kernel<false>; iq4xs_kernel<false><<<grid_for(k, tiles, ctx, 0, IQ4XS_THREADS), IQ4XS_THREADS, 0, st>>>(a); }
         break;
     }
     default:
