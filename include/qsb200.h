@@ -89,6 +89,43 @@ int qs_row_bytes(int ggml_type, int64_t k, int64_t* out_bytes);
 int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_rows, int64_t k,
                 const float* qw, void* dst, int64_t dst_row_bytes, void* stream);
 
+/*
+ * Decode n_rows rows of packed blocks to float32: the GGUF dequantization of every type
+ * above, value for value what gguf-py's gguf.quants.dequantize returns (the decode the
+ * reference's correctness harness compares with, tools/dev_harness.py:108-109).
+ *   src             device pointer; row r starts at src + r * src_row_bytes
+ *   src_row_bytes   >= qs_row_bytes(type, k)
+ *   dst             device pointer, 16-byte aligned; row r at dst + r * dst_row_stride
+ *   dst_row_stride  elements, a multiple of 4, >= k
+ */
+int qs_dequantize(int ggml_type, const void* src, int64_t src_row_bytes, int64_t n_rows, int64_t k,
+                  float* dst, int64_t dst_row_stride, void* stream);
+
+/*
+ * Squared error of every decoded block against the source values, in double:
+ *   err[r * (k / qk) + j] = sum over the values of block j of row r of w * (deq - x)^2,
+ *   w = qw[column], or 1 when qw is NULL.
+ * The per-block form of the harness's decoded-error check (tools/dev_harness.py:110-112).
+ *   blocks, blocks_row_bytes   as src / src_row_bytes of qs_dequantize
+ *   x, x_type                  n_rows x k source values (F32 / F16 / BF16), rows
+ *                              contiguous, 16-byte aligned
+ *   qw                         k float32 weights (16-byte aligned) or NULL
+ *   err                        device pointer to n_rows * (k / qk) doubles
+ */
+int qs_block_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x, int x_type,
+                   int64_t n_rows, int64_t k, const float* qw, double* err, void* stream);
+
+/*
+ * Error sums over the whole tensor, in double and in a fixed order (the same bits on
+ * every call on the same GPU model):
+ *   out[0] = sum w * (deq - x)^2, out[1] = sum (deq - x)^2   (out: 2 device doubles)
+ * out[1] / (n_rows * k) is the `((dq - xf) ** 2).mean()` of tools/dev_harness.py:110-111.
+ * Arguments as qs_block_error. Scratch for the per-CTA partial sums comes from the
+ * stream-ordered allocator (cudaMallocAsync / cudaFreeAsync on `stream`).
+ */
+int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x, int x_type,
+                    int64_t n_rows, int64_t k, const float* qw, double* out, void* stream);
+
 /* Message of the calling thread's last failure ("" if none). */
 const char* qs_last_error(void);
 

@@ -73,8 +73,9 @@ int ensure_device(int device, DeviceState** out) {
 
 }  // namespace
 
-extern "C" {
 #define QS_API __attribute__((visibility("default")))
+
+extern "C" {
 
 QS_API int qs_version(void) { return QSB200_VERSION; }
 
@@ -113,6 +114,55 @@ QS_API int qs_init(int device) {
     if (prev != device) cudaSetDevice(prev);
     return rc;
 }
+
+}  // extern "C"
+
+namespace {
+
+// Make the device that owns `p` current (the runtime's current device may belong to
+// another runtime instance in the process, e.g. the one torch links) and prepare it.
+int device_of(const void* p, const char* what, int* device, DeviceState** st) {
+    cudaPointerAttributes pa;
+    cudaError_t e = cudaPointerGetAttributes(&pa, p);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+    if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+        return fail(QS_EINVAL, "%s is not device memory", what);
+    int cur = -1;
+    if ((e = cudaGetDevice(&cur)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != pa.device && (e = cudaSetDevice(pa.device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    *device = pa.device;
+    return ensure_device(pa.device, st);
+}
+
+// Checks shared by the decode entry points; fills the kernel call.
+int check_decode(int ggml_type, const void* blocks, int64_t blocks_row_bytes, int64_t n_rows, int64_t k,
+                 qs::DqCall& c) {
+    const TypeInfo* ti = find_type(ggml_type);
+    if (!ti) return fail(QS_ENOTSUP, "ggml type %d is not supported", ggml_type);
+    if (k <= 0 || k % ti->qk) return fail(QS_EINVAL, "row length %lld is not a positive multiple of %d", (long long)k, ti->qk);
+    if (n_rows < 0) return fail(QS_EINVAL, "negative row count");
+    const int64_t row_bytes = k / ti->qk * ti->bytes;
+    if (blocks_row_bytes < row_bytes)
+        return fail(QS_EINVAL, "block row stride %lld < packed row size %lld", (long long)blocks_row_bytes, (long long)row_bytes);
+    memset(&c, 0, sizeof(c));
+    c.blocks = blocks;
+    c.blocks_row_bytes = blocks_row_bytes;
+    c.n_rows = n_rows;
+    c.k = k;
+    return QS_OK;
+}
+
+int check_source(const void* x, int x_type, const float* qw) {
+    if (x_type != QS_SRC_F32 && x_type != QS_SRC_F16 && x_type != QS_SRC_BF16)
+        return fail(QS_EINVAL, "source type %d is not F32/F16/BF16", x_type);
+    if (!x) return fail(QS_EINVAL, "null source rows");
+    if (((uintptr_t)x & 15) || (qw && ((uintptr_t)qw & 15))) return fail(QS_EINVAL, "x and qw must be 16-byte aligned");
+    return QS_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_rows, int64_t k, const float* qw,
                 void* dst, int64_t dst_row_bytes, void* stream) {
@@ -160,6 +210,73 @@ QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_r
     e = is_iq(ggml_type) ? qs::launch_iq(ggml_type, a, ctx, d->iq) : qs::launch_kquant(ggml_type, a, ctx);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return QS_OK;
+}
+
+QS_API int qs_dequantize(int ggml_type, const void* src, int64_t src_row_bytes, int64_t n_rows, int64_t k, float* dst,
+                         int64_t dst_row_stride, void* stream) {
+    qs::DqCall c;
+    int rc = check_decode(ggml_type, src, src_row_bytes, n_rows, k, c);
+    if (rc) return rc;
+    if (dst_row_stride < k || dst_row_stride % 4) return fail(QS_EINVAL, "dst_row_stride %lld must be >= k and a multiple of 4", (long long)dst_row_stride);
+    if (n_rows == 0) return QS_OK;
+    if (!src || !dst) return fail(QS_EINVAL, "null src or dst");
+    if ((uintptr_t)dst & 15) return fail(QS_EINVAL, "dst must be 16-byte aligned");
+    int device;
+    DeviceState* d;
+    if ((rc = device_of(src, "src", &device, &d))) return rc;
+    c.dst = dst;
+    c.dst_stride = dst_row_stride;
+    qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
+    cudaError_t e = qs::launch_dequant(ggml_type, c, ctx, d->iq);
+    return e == cudaSuccess ? QS_OK : cuda_fail(e, "dequantize launch");
+}
+
+QS_API int qs_block_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x, int x_type,
+                          int64_t n_rows, int64_t k, const float* qw, double* err, void* stream) {
+    qs::DqCall c;
+    int rc = check_decode(ggml_type, blocks, blocks_row_bytes, n_rows, k, c);
+    if (rc) return rc;
+    if (n_rows == 0) return QS_OK;
+    if ((rc = check_source(x, x_type, qw))) return rc;
+    if (!blocks || !err) return fail(QS_EINVAL, "null blocks or err");
+    int device;
+    DeviceState* d;
+    if ((rc = device_of(blocks, "blocks", &device, &d))) return rc;
+    c.x = x;
+    c.x_type = x_type;
+    c.qw = qw;
+    c.err = err;
+    qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
+    cudaError_t e = qs::launch_block_error(ggml_type, c, ctx, d->iq);
+    return e == cudaSuccess ? QS_OK : cuda_fail(e, "block error launch");
+}
+
+QS_API int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x, int x_type,
+                           int64_t n_rows, int64_t k, const float* qw, double* out, void* stream) {
+    qs::DqCall c;
+    int rc = check_decode(ggml_type, blocks, blocks_row_bytes, n_rows, k, c);
+    if (rc) return rc;
+    if (!out) return fail(QS_EINVAL, "null out");
+    if (n_rows > 0) {
+        if ((rc = check_source(x, x_type, qw))) return rc;
+        if (!blocks) return fail(QS_EINVAL, "null blocks");
+    }
+    int device;
+    DeviceState* d;
+    if ((rc = device_of(out, "out", &device, &d))) return rc;
+    c.x = x;
+    c.x_type = x_type;
+    c.qw = qw;
+    qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
+    const int np = qs::dq_partial_count(ggml_type, n_rows, k, ctx);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void* partial = nullptr;
+    cudaError_t e = cudaMallocAsync(&partial, (size_t)np * 2 * sizeof(double), st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (partial sums)");
+    e = qs::launch_tensor_error(ggml_type, c, static_cast<double*>(partial), np, out, ctx, d->iq);
+    cudaError_t ef = cudaFreeAsync(partial, st);
+    if (e != cudaSuccess) return cuda_fail(e, "tensor error launch");
+    return ef == cudaSuccess ? QS_OK : cuda_fail(ef, "cudaFreeAsync (partial sums)");
 }
 
 }  // extern "C"

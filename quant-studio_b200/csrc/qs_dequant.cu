@@ -1,0 +1,453 @@
+// Block decode (GGUF dequantization) and the decode-error checkers (sm_100a).
+//
+// The decode of every block format restates gguf-py's numpy dequantizers
+// (gguf/quants.py, gguf 0.19.0: Q4_0 / Q2_K / Q3_K / Q4_K / Q5_K / Q6_K / IQ2_XXS /
+// IQ2_XS / IQ2_S / IQ3_XXS / IQ3_S / IQ4_XS .dequantize_blocks), which is what the
+// reference's correctness harness decodes with (tools/dev_harness.py:108-109): the same
+// float32 operations in the same order, so the values are bit-identical. The checkers
+// measure what that harness measures next (tools/dev_harness.py:110-112), the squared
+// error of the decoded values against the source rows, with optional importance
+// weights, accumulated in double.
+//
+// Mapping: a CTA of 256 threads takes a tile of blocks (8 superblocks, or 64 Q4_0
+// blocks), copies their bytes to shared memory with 16-byte loads, and each thread
+// decodes 8 consecutive values of one block. HBM-bound: the decode writes 4 bytes per
+// value, the checkers read the source rows (2 or 4 bytes per value).
+#include "qs_kernels.h"
+
+namespace qs {
+
+namespace {
+
+constexpr int DQ_THREADS = 256;
+
+enum DqMode { DQ_DECODE, DQ_BLOCK_ERR, DQ_SUM_ERR };
+
+__device__ __forceinline__ float f16_at(const uint8_t* p) { return f16_val((uint16_t)(p[0] | (p[1] << 8))); }
+__device__ __forceinline__ uint32_t u32_at(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+// ksigns[i] of the IQ2/IQ3 formats: 7 sign bits plus their parity in bit 7
+__device__ __forceinline__ uint32_t ksign(uint32_t i) { return i | ((__popc(i) & 1u) << 7); }
+__device__ __forceinline__ float sgn(uint32_t bits, int j) { return (bits >> j) & 1u ? -1.0f : 1.0f; }
+
+// Level -> grid value maps of the IQ dequant grids (gguf IQ*.grid_map).
+__device__ __forceinline__ float iq2_val(int l) { return l == 0 ? 8.0f : (l == 1 ? 25.0f : 43.0f); }
+__device__ __forceinline__ float iq3xxs_val(int l) { return l == 7 ? 62.0f : (float)(4 + 8 * l); }
+__device__ __forceinline__ float iq3s_val(int l) { return (float)(2 * l + 1); }
+
+__constant__ int8_t c_kvalues[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+template <int T> struct Dq;
+
+// Q4_0 (gguf Q4_0.dequantize_blocks): d * (q - 8); bytes hold values j (low) and j + 16 (high)
+template <> struct Dq<QS_Q4_0> {
+    static constexpr int QK = 32, BB = 18;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b);
+        const int p = 8 * t;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int q = p < 16 ? (b[2 + p + i] & 0xF) : (b[2 + p - 16 + i] >> 4);
+            v[i] = d * (float)(q - 8);
+        }
+    }
+};
+
+// Q2_K: scales[16] qs[64] d dmin; value e: (d * (sc & 15)) * q - dmin * (sc >> 4)
+template <> struct Dq<QS_Q2_K> {
+    static constexpr int QK = 256, BB = 84;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b + 80), dmin = f16_at(b + 82);
+        const int e0 = 8 * t, sc = b[e0 / 16];
+        const float dl = d * (float)(sc & 0xF), ml = dmin * (float)(sc >> 4);
+        const int h = e0 / 128, s = (e0 % 128) / 32, l0 = e0 % 32;
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = dl * (float)((b[16 + 32 * h + l0 + i] >> (2 * s)) & 3) - ml;
+    }
+};
+
+// Q3_K: hmask[32] qs[64] scales[12] d; value e: (d * (sc - 32)) * (ql - 4 * !hbit)
+template <> struct Dq<QS_Q3_K> {
+    static constexpr int QK = 256, BB = 110;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b + 108);
+        const int e0 = 8 * t, g = e0 / 16;
+        const uint8_t* sc = b + 96;
+        const int ls = (sc[g % 8] >> (4 * (g / 8))) & 0xF, hs = (sc[8 + g % 4] >> (2 * (g / 4))) & 3;
+        const float dl = d * (float)((int)(int8_t)(uint8_t)(ls | (hs << 4)) - 32);
+        const int h = e0 / 128, s = (e0 % 128) / 32, s8 = e0 / 32, l0 = e0 % 32;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int ql = (b[32 + 32 * h + l0 + i] >> (2 * s)) & 3;
+            const int qh = ((b[l0 + i] >> s8) & 1) ^ 1;
+            v[i] = dl * (float)(ql - (qh << 2));
+        }
+    }
+};
+
+// 6-bit scale / min j of the Q4_K / Q5_K scale block (gguf Q4_K.get_scale_min)
+__device__ __forceinline__ void k_scale_min(const uint8_t* s, int j, int& sc, int& mn) {
+    if (j < 4) {
+        sc = s[j] & 0x3F;
+        mn = s[4 + j] & 0x3F;
+    } else {
+        sc = (s[8 + j - 4] & 0x0F) | ((s[j - 4] >> 2) & 0x30);
+        mn = (s[8 + j - 4] >> 4) | ((s[4 + j - 4] >> 2) & 0x30);
+    }
+}
+
+// Q4_K: d dmin scales[12] qs[128]; value e: (d * sc) * q - dmin * m
+template <> struct Dq<QS_Q4_K> {
+    static constexpr int QK = 256, BB = 144;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b), dmin = f16_at(b + 2);
+        const int e0 = 8 * t, sub = e0 / 32, c = e0 / 64, s = (e0 % 64) / 32, l0 = e0 % 32;
+        int sc, mn;
+        k_scale_min(b + 4, sub, sc, mn);
+        const float dl = d * (float)sc, ml = dmin * (float)mn;
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = dl * (float)((b[16 + 32 * c + l0 + i] >> (4 * s)) & 0xF) - ml;
+    }
+};
+
+// Q5_K: d dmin scales[12] qh[32] qs[128]
+template <> struct Dq<QS_Q5_K> {
+    static constexpr int QK = 256, BB = 176;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b), dmin = f16_at(b + 2);
+        const int e0 = 8 * t, sub = e0 / 32, c = e0 / 64, s = (e0 % 64) / 32, l0 = e0 % 32;
+        int sc, mn;
+        k_scale_min(b + 4, sub, sc, mn);
+        const float dl = d * (float)sc, ml = dmin * (float)mn;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int q = ((b[48 + 32 * c + l0 + i] >> (4 * s)) & 0xF) | (((b[16 + l0 + i] >> sub) & 1) << 4);
+            v[i] = dl * (float)q - ml;
+        }
+    }
+};
+
+// Q6_K: ql[128] qh[64] scales[16] (int8) d; value e: (d * sc) * (q - 32)
+template <> struct Dq<QS_Q6_K> {
+    static constexpr int QK = 256, BB = 210;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b + 208);
+        const int e0 = 8 * t;
+        const float dl = d * (float)(int8_t)b[192 + e0 / 16];
+        const int c = e0 / 128, sl = (e0 % 128) / 64, ll = e0 % 64, sh = (e0 % 128) / 32, lh = e0 % 32;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int ql = (b[64 * c + ll + i] >> (4 * sl)) & 0xF;
+            const int qh = (b[128 + 32 * c + lh + i] >> (2 * sh)) & 3;
+            v[i] = dl * (float)((int)(int8_t)(uint8_t)(ql | (qh << 4)) - 32);
+        }
+    }
+};
+
+// IQ2_XXS: d, 8 x (4 grid bytes, u32 of 4 x 7 sign bits | scale << 28)
+template <> struct Dq<QS_IQ2_XXS> {
+    static constexpr int QK = 256, BB = 66;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
+        const float d = f16_at(b);
+        const int g = t / 4, s = t % 4;
+        const uint32_t w1 = u32_at(b + 2 + 8 * g + 4);
+        const float db = (d * (0.5f + (float)(w1 >> 28))) * 0.25f;
+        const uint32_t sg = ksign((w1 >> (7 * s)) & 127);
+        const int code = __ldg(kgrid + b[2 + 8 * g + s]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = (db * iq2_val((code >> (2 * j)) & 3)) * sgn(sg, j);
+    }
+};
+
+// IQ2_XS: d, 32 x u16 (9-bit grid index | 7-bit sign index << 9), 8 bytes of 4-bit scales
+template <> struct Dq<QS_IQ2_XS> {
+    static constexpr int QK = 256, BB = 74;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
+        const float d = f16_at(b);
+        const int q16 = b[2 + 2 * t] | (b[3 + 2 * t] << 8);
+        const int sc = (b[66 + t / 4] >> (4 * ((t / 2) & 1))) & 0xF;
+        const float db = (d * (0.5f + (float)sc)) * 0.25f;
+        const uint32_t sg = ksign((uint32_t)q16 >> 9);
+        const int code = __ldg(kgrid + (q16 & 511));
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = (db * iq2_val((code >> (2 * j)) & 3)) * sgn(sg, j);
+    }
+};
+
+// IQ2_S: d, qs[32], signs[32], qh[8] (2 high index bits each), scales[8]
+template <> struct Dq<QS_IQ2_S> {
+    static constexpr int QK = 256, BB = 82;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
+        const float d = f16_at(b);
+        const int sc = (b[74 + t / 4] >> (4 * ((t / 2) & 1))) & 0xF;
+        const float db = (d * (0.5f + (float)sc)) * 0.25f;
+        const int gi = b[2 + t] | (((b[66 + t / 4] >> (2 * (t % 4))) & 3) << 8);
+        const uint32_t sg = b[34 + t];
+        const int code = __ldg(kgrid + gi);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = (db * iq2_val((code >> (2 * j)) & 3)) * sgn(sg, j);
+    }
+};
+
+// IQ3_XXS: d, qs[64] grid bytes (4 values each), 8 x u32 (4 x 7 sign bits | scale << 28)
+template <> struct Dq<QS_IQ3_XXS> {
+    static constexpr int QK = 256, BB = 98;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
+        const float d = f16_at(b);
+        const int g = t / 4, s = t % 4;
+        const uint32_t w = u32_at(b + 66 + 4 * g);
+        const float db = (d * (0.5f + (float)(w >> 28))) * 0.5f;
+        const uint32_t sg = ksign((w >> (7 * s)) & 127);
+        const int c0 = __ldg(kgrid + b[2 + 2 * t]), c1 = __ldg(kgrid + b[3 + 2 * t]);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            v[j] = (db * iq3xxs_val((c0 >> (3 * j)) & 7)) * sgn(sg, j);
+            v[4 + j] = (db * iq3xxs_val((c1 >> (3 * j)) & 7)) * sgn(sg, 4 + j);
+        }
+    }
+};
+
+// IQ3_S: d, qs[64], qh[8] (high index bit), signs[32], scales[4]; db = d * (1 + 2 * sc)
+template <> struct Dq<QS_IQ3_S> {
+    static constexpr int QK = 256, BB = 110;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
+        const float d = f16_at(b);
+        const int g = t / 4;
+        const int sc = (b[106 + g / 2] >> (4 * (g & 1))) & 0xF;
+        const float db = d * (float)(1 + 2 * sc);
+        const uint32_t sg = b[74 + t];
+        const int k0 = 2 * t, k1 = 2 * t + 1;
+        const int g0 = b[2 + k0] | (((b[66 + k0 / 8] >> (k0 % 8)) & 1) << 8);
+        const int g1 = b[2 + k1] | (((b[66 + k1 / 8] >> (k1 % 8)) & 1) << 8);
+        const int c0 = __ldg(kgrid + g0), c1 = __ldg(kgrid + g1);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            v[j] = (db * iq3s_val((c0 >> (3 * j)) & 7)) * sgn(sg, j);
+            v[4 + j] = (db * iq3s_val((c1 >> (3 * j)) & 7)) * sgn(sg, 4 + j);
+        }
+    }
+};
+
+// IQ4_XS: d, scales_h (u16), scales_l[4], qs[128]; value: (d * (sc - 32)) * kvalues[q]
+template <> struct Dq<QS_IQ4_XS> {
+    static constexpr int QK = 256, BB = 136;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b);
+        const int i = t / 4, u = (t % 4) / 2, j0 = 8 * (t % 2);
+        const int sh = b[2] | (b[3] << 8);
+        const int ls = (b[4 + i / 2] >> (4 * (i & 1))) & 0xF, hs = (sh >> (2 * i)) & 3;
+        const float dl = d * (float)((int)(int8_t)(uint8_t)(ls | (hs << 4)) - 32);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = dl * (float)c_kvalues[(b[8 + 16 * i + j0 + j] >> (4 * u)) & 0xF];
+    }
+};
+
+struct DqArgs {
+    const uint8_t* src;       // packed rows
+    int64_t src_row_bytes;
+    int64_t n_rows, k, nblk_row, nblk;
+    float* dst;               // DQ_DECODE
+    int64_t dst_stride;       // elements
+    const void* x;            // DQ_*_ERR: source rows, n_rows x k contiguous
+    int x_type;
+    const float* qw;          // k weights or null
+    double* err;              // DQ_BLOCK_ERR: one per block
+    double* partial;          // DQ_SUM_ERR: 2 per CTA (weighted, plain)
+    const uint16_t* kgrid;    // IQ codebook of the type (grid index -> code)
+};
+
+__device__ __forceinline__ void load_x8(const void* base, int64_t e0, int src, float* v) { load_row<8>(base, e0, src, v); }
+
+template <int TYPE, int MODE>
+__global__ void __launch_bounds__(DQ_THREADS) dq_kernel(DqArgs a) {
+    using D = Dq<TYPE>;
+    constexpr int TPB = D::QK / 8, BPT = DQ_THREADS / TPB;  // threads per block, blocks per tile
+    __shared__ __align__(16) uint8_t s_blk[BPT * D::BB + 16];
+    __shared__ double s_red[2][DQ_THREADS / 32];
+    const int tid = threadIdx.x, lb = tid / TPB, t = tid % TPB;
+    const bool packed = a.src_row_bytes == a.nblk_row * D::BB;
+    double acc_w = 0.0, acc = 0.0;
+
+    for (int64_t tile = blockIdx.x; tile * BPT < a.nblk; tile += gridDim.x) {
+        const int64_t b0 = tile * BPT;
+        const int nb = (int)min((int64_t)BPT, a.nblk - b0);
+        if (packed) {
+            // the tile is one contiguous span of nb * BB bytes
+            const uint8_t* g = a.src + b0 * D::BB;
+            const int nbytes = nb * D::BB;
+            const int head = (int)((16 - ((uintptr_t)g & 15)) & 15) < nbytes ? (int)((16 - ((uintptr_t)g & 15)) & 15) : nbytes;
+            for (int i = tid; i < head; i += DQ_THREADS) s_blk[i] = __ldg(g + i);
+            const int body = (nbytes - head) / 16;
+            const uint4* g4 = reinterpret_cast<const uint4*>(g + head);
+            for (int i = tid; i < body; i += DQ_THREADS) {
+                const uint4 w = __ldg(g4 + i);
+                uint8_t* s = s_blk + head + 16 * i;
+                const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 16; j++) s[j] = (uint8_t)(w4[j >> 2] >> (8 * (j & 3)));
+            }
+            for (int i = head + 16 * body + tid; i < nbytes; i += DQ_THREADS) s_blk[i] = __ldg(g + i);
+        } else {
+            for (int i = tid; i < nb * D::BB; i += DQ_THREADS) {
+                const int64_t bb = b0 + i / D::BB;
+                const int64_t row = bb / a.nblk_row, col = bb - row * a.nblk_row;
+                s_blk[i] = __ldg(a.src + row * a.src_row_bytes + col * D::BB + i % D::BB);
+            }
+        }
+        __syncthreads();
+        if (lb < nb) {
+            float v[8];
+            D::decode(s_blk + lb * D::BB, t, a.kgrid, v);
+            const int64_t b = b0 + lb, row = b / a.nblk_row;
+            const int64_t col = (b - row * a.nblk_row) * D::QK + 8 * t;
+            if (MODE == DQ_DECODE) {
+                float4* o = reinterpret_cast<float4*>(a.dst + row * a.dst_stride + col);
+                o[0] = make_float4(v[0], v[1], v[2], v[3]);
+                o[1] = make_float4(v[4], v[5], v[6], v[7]);
+            } else {
+                float xv[8], w[8];
+                load_x8(a.x, row * a.k + col, a.x_type, xv);
+                if (a.qw) load_f32<8>(a.qw + col, w);
+                double ew = 0.0, e2 = 0.0;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const double e = (double)v[i] - (double)xv[i];
+                    const double ee = e * e;
+                    e2 += ee;
+                    ew += a.qw ? (double)w[i] * ee : ee;
+                }
+                if (MODE == DQ_BLOCK_ERR) {
+                    // the TPB threads of the block are adjacent lanes; fixed xor tree
+#pragma unroll
+                    for (int o = TPB / 2; o > 0; o >>= 1) ew += __shfl_xor_sync(TPB == 32 ? 0xffffffffu : (0xFu << (tid & 28)), ew, o);
+                    if (t == 0) a.err[b] = ew;
+                } else {
+                    acc_w += ew;
+                    acc += e2;
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (MODE == DQ_SUM_ERR) {
+        // CTA partial: xor tree within each warp, then warps in order
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            acc_w += __shfl_xor_sync(0xffffffffu, acc_w, o);
+            acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        }
+        if ((tid & 31) == 0) { s_red[0][tid >> 5] = acc_w; s_red[1][tid >> 5] = acc; }
+        __syncthreads();
+        if (tid == 0) {
+            double sw = 0.0, s = 0.0;
+            for (int i = 0; i < DQ_THREADS / 32; i++) { sw += s_red[0][i]; s += s_red[1][i]; }
+            a.partial[2 * blockIdx.x] = sw;
+            a.partial[2 * blockIdx.x + 1] = s;
+        }
+    }
+}
+
+// Sum the per-CTA partials in a fixed order: thread i adds partials i, i + 256, ...,
+// then a tree over the 256 threads. out[0] weighted, out[1] plain.
+__global__ void __launch_bounds__(DQ_THREADS) dq_finish_kernel(const double* partial, int n, double* out) {
+    __shared__ double s[2][DQ_THREADS];
+    const int tid = threadIdx.x;
+    double sw = 0.0, sp = 0.0;
+    for (int i = tid; i < n; i += DQ_THREADS) { sw += partial[2 * i]; sp += partial[2 * i + 1]; }
+    s[0][tid] = sw;
+    s[1][tid] = sp;
+    __syncthreads();
+    for (int h = DQ_THREADS / 2; h > 0; h >>= 1) {
+        if (tid < h) { s[0][tid] += s[0][tid + h]; s[1][tid] += s[1][tid + h]; }
+        __syncthreads();
+    }
+    if (tid == 0) { out[0] = s[0][0]; out[1] = s[1][0]; }
+}
+
+template <int TYPE, int MODE>
+cudaError_t launch_dq_t(const DqArgs& a, const LaunchCtx& ctx, int grid) {
+    dq_kernel<TYPE, MODE><<<grid, DQ_THREADS, 0, ctx.stream>>>(a);
+    return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_dq_mode(int type, const DqArgs& a, const LaunchCtx& ctx, int grid) {
+    switch (type) {
+    case QS_Q4_0: return launch_dq_t<QS_Q4_0, MODE>(a, ctx, grid);
+    case QS_Q2_K: return launch_dq_t<QS_Q2_K, MODE>(a, ctx, grid);
+    case QS_Q3_K: return launch_dq_t<QS_Q3_K, MODE>(a, ctx, grid);
+    case QS_Q4_K: return launch_dq_t<QS_Q4_K, MODE>(a, ctx, grid);
+    case QS_Q5_K: return launch_dq_t<QS_Q5_K, MODE>(a, ctx, grid);
+    case QS_Q6_K: return launch_dq_t<QS_Q6_K, MODE>(a, ctx, grid);
+    case QS_IQ2_XXS: return launch_dq_t<QS_IQ2_XXS, MODE>(a, ctx, grid);
+    case QS_IQ2_XS: return launch_dq_t<QS_IQ2_XS, MODE>(a, ctx, grid);
+    case QS_IQ2_S: return launch_dq_t<QS_IQ2_S, MODE>(a, ctx, grid);
+    case QS_IQ3_XXS: return launch_dq_t<QS_IQ3_XXS, MODE>(a, ctx, grid);
+    case QS_IQ3_S: return launch_dq_t<QS_IQ3_S, MODE>(a, ctx, grid);
+    case QS_IQ4_XS: return launch_dq_t<QS_IQ4_XS, MODE>(a, ctx, grid);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+int block_qk(int type) { return type == QS_Q4_0 ? 32 : 256; }
+
+DqArgs make_args(int type, const DqCall& c, const IqTables* t) {
+    DqArgs a;
+    a.src = static_cast<const uint8_t*>(c.blocks);
+    a.src_row_bytes = c.blocks_row_bytes;
+    a.n_rows = c.n_rows;
+    a.k = c.k;
+    a.nblk_row = c.k / block_qk(type);
+    a.nblk = c.n_rows * a.nblk_row;
+    a.dst = c.dst;
+    a.dst_stride = c.dst_stride;
+    a.x = c.x;
+    a.x_type = c.x_type;
+    a.qw = c.qw;
+    a.err = c.err;
+    a.partial = nullptr;
+    a.kgrid = iq_kgrid(t, type);
+    return a;
+}
+
+// CTAs for a pass over nblk blocks: tiles of 8 superblocks (64 Q4_0 blocks), capped at
+// 8 resident CTAs per SM.
+int dq_grid(int type, int64_t nblk, const LaunchCtx& ctx) {
+    const int bpt = DQ_THREADS / (block_qk(type) / 8);
+    const int64_t tiles = (nblk + bpt - 1) / bpt;
+    const int64_t cap = (int64_t)ctx.num_sms * 8;
+    return (int)(tiles < cap ? (tiles > 0 ? tiles : 1) : cap);
+}
+
+}  // namespace
+
+int dq_partial_count(int type, int64_t n_rows, int64_t k, const LaunchCtx& ctx) {
+    return dq_grid(type, n_rows * (k / block_qk(type)), ctx);
+}
+
+cudaError_t launch_dequant(int type, const DqCall& c, const LaunchCtx& ctx, const IqTables* t) {
+    DqArgs a = make_args(type, c, t);
+    if (a.nblk == 0) return cudaSuccess;
+    return launch_dq_mode<DQ_DECODE>(type, a, ctx, dq_grid(type, a.nblk, ctx));
+}
+
+cudaError_t launch_block_error(int type, const DqCall& c, const LaunchCtx& ctx, const IqTables* t) {
+    DqArgs a = make_args(type, c, t);
+    if (a.nblk == 0) return cudaSuccess;
+    return launch_dq_mode<DQ_BLOCK_ERR>(type, a, ctx, dq_grid(type, a.nblk, ctx));
+}
+
+cudaError_t launch_tensor_error(int type, const DqCall& c, double* partial, int npartial, double* out,
+                                const LaunchCtx& ctx, const IqTables* t) {
+    DqArgs a = make_args(type, c, t);
+    a.partial = partial;
+    const int grid = dq_grid(type, a.nblk, ctx);
+    if (grid > npartial) return cudaErrorInvalidValue;
+    cudaError_t e = a.nblk ? launch_dq_mode<DQ_SUM_ERR>(type, a, ctx, grid) : cudaSuccess;
+    if (e != cudaSuccess) return e;
+    dq_finish_kernel<<<1, DQ_THREADS, 0, ctx.stream>>>(partial, a.nblk ? grid : 0, out);
+    return cudaGetLastError();
+}
+
+}  // namespace qs

@@ -138,6 +138,17 @@ cudaError_t iq_tables_create(IqTables** out) {
     return cudaSuccess;
 }
 
+const uint16_t* iq_kgrid(const IqTables* t, int type) {
+    switch (type) {
+    case QS_IQ2_XXS: return t->g[G_IQ2XXS].kgrid;
+    case QS_IQ2_XS: return t->g[G_IQ2XS].kgrid;
+    case QS_IQ2_S: return t->g[G_IQ2S].kgrid;
+    case QS_IQ3_XXS: return t->g[G_IQ3XXS].kgrid;
+    case QS_IQ3_S: return t->g[G_IQ3S].kgrid;
+    default: return nullptr;
+    }
+}
+
 void iq_tables_destroy(IqTables* t) {
     if (t) {
         cudaFree(t->mem);

@@ -36,5 +36,28 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx);
 cudaError_t launch_iq(int type, const QuantArgs& a, const LaunchCtx& ctx, const IqTables* t);
 cudaError_t iq_tables_create(IqTables** out);  // uploads to the current device
 void iq_tables_destroy(IqTables* t);
+const uint16_t* iq_kgrid(const IqTables* t, int type);  // IQ codebook (grid index -> code), else null
+
+// One decode / decode-error pass (qs_dequant.cu).
+struct DqCall {
+    const void* blocks;        // packed rows, row r at blocks + r * blocks_row_bytes
+    int64_t blocks_row_bytes;
+    int64_t n_rows, k;
+    float* dst;                // decode: row r at dst + r * dst_stride
+    int64_t dst_stride;
+    const void* x;             // error passes: n_rows x k source values of x_type
+    int x_type;
+    const float* qw;           // k weights or null
+    double* err;               // block error: one double per block
+};
+
+cudaError_t launch_dequant(int type, const DqCall& c, const LaunchCtx& ctx, const IqTables* t);
+cudaError_t launch_block_error(int type, const DqCall& c, const LaunchCtx& ctx, const IqTables* t);
+// Number of per-CTA partials (2 doubles each) launch_tensor_error writes.
+int dq_partial_count(int type, int64_t n_rows, int64_t k, const LaunchCtx& ctx);
+// Error sums over the tensor: CTA partials into `partial` (room for npartial), then
+// out[0] = sum w (deq - x)^2, out[1] = sum (deq - x)^2 in a fixed order.
+cudaError_t launch_tensor_error(int type, const DqCall& c, double* partial, int npartial, double* out,
+                                const LaunchCtx& ctx, const IqTables* t);
 
 }  // namespace qs

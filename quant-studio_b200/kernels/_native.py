@@ -58,6 +58,9 @@ def lib() -> ctypes.CDLL:
             L.qs_block_info.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]
             L.qs_row_bytes.argtypes = [ctypes.c_int, c_i64, ctypes.POINTER(c_i64)]
             L.qs_quantize.argtypes = [ctypes.c_int, c_vp, ctypes.c_int, c_i64, c_i64, c_vp, c_vp, c_i64, c_vp]
+            L.qs_dequantize.argtypes = [ctypes.c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]
+            L.qs_block_error.argtypes = [ctypes.c_int, c_vp, c_i64, c_vp, ctypes.c_int, c_i64, c_i64, c_vp, c_vp, c_vp]
+            L.qs_tensor_error.argtypes = [ctypes.c_int, c_vp, c_i64, c_vp, ctypes.c_int, c_i64, c_i64, c_vp, c_vp, c_vp]
             L.qs_last_error.restype = ctypes.c_char_p
             _lib = L
     return _lib
@@ -112,3 +115,63 @@ def quantize(ggml_type: int, x: torch.Tensor, qw: torch.Tensor | None) -> torch.
     if qw is not None:
         qw = qw.to(device=x.device, dtype=torch.float32).contiguous()
     return quantize_into(ggml_type, x, qw, out)
+
+
+def _blocks_arg(blocks: torch.Tensor, ggml_type: int) -> tuple[int, int]:
+    """(n_rows, k) of a (n_rows, row_bytes) uint8 block tensor (row stride may exceed row_bytes)."""
+    if blocks.device.type != "cuda":
+        raise QsError(QS_EINVAL, f"blocks are on {blocks.device}; qsb200 runs on CUDA devices only")
+    if blocks.dtype != torch.uint8 or blocks.dim() != 2 or blocks.stride(1) != 1:
+        raise QsError(QS_EINVAL, "blocks must be a row-major (n_rows, bytes) uint8 tensor")
+    qk, nb = block_info(ggml_type)
+    if blocks.shape[1] % nb:
+        raise QsError(QS_EINVAL, f"row of {blocks.shape[1]} bytes is not a whole number of {nb}-byte blocks")
+    return blocks.shape[0], blocks.shape[1] // nb * qk
+
+
+def dequantize(blocks: torch.Tensor, ggml_type: int) -> torch.Tensor:
+    """Decode (n_rows, row_bytes) packed blocks to a new (n_rows, k) float32 tensor on the
+    same device: the values gguf.quants.dequantize returns for the same bytes."""
+    n, k = _blocks_arg(blocks, ggml_type)
+    out = torch.empty((n, k + (-k) % 4), dtype=torch.float32, device=blocks.device)
+    stream = torch.cuda.current_stream(blocks.device)
+    with torch.cuda.device(blocks.device):
+        check(lib().qs_dequantize(int(ggml_type), blocks.data_ptr(), blocks.stride(0), n, k,
+                                  out.data_ptr(), out.stride(0), stream.cuda_stream))
+    return out[:, :k]
+
+
+def _error_args(blocks: torch.Tensor, ggml_type: int, x: torch.Tensor, qw: torch.Tensor | None):
+    n, k = _blocks_arg(blocks, ggml_type)
+    if x.device != blocks.device or x.dtype not in SRC_IDS or not x.is_contiguous() or tuple(x.shape) != (n, k):
+        raise QsError(QS_EINVAL, f"x must be a contiguous ({n}, {k}) f32/f16/bf16 tensor on the blocks' device")
+    qptr = None
+    if qw is not None:
+        if qw.device != x.device or qw.dtype != torch.float32 or not qw.is_contiguous() or qw.numel() < k:
+            raise QsError(QS_EINVAL, "qw must be a contiguous float32 tensor of >= k values on the blocks' device")
+        qptr = qw.data_ptr()
+    return n, k, qptr
+
+
+def block_error(blocks: torch.Tensor, ggml_type: int, x: torch.Tensor, qw: torch.Tensor | None = None) -> torch.Tensor:
+    """(n_rows, k // qk) float64 tensor: per block, sum of qw * (decoded - x)^2 (qw = 1 if None)."""
+    n, k, qptr = _error_args(blocks, ggml_type, x, qw)
+    qk, _ = block_info(ggml_type)
+    err = torch.empty((n, k // qk), dtype=torch.float64, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    with torch.cuda.device(x.device):
+        check(lib().qs_block_error(int(ggml_type), blocks.data_ptr(), blocks.stride(0), x.data_ptr(), SRC_IDS[x.dtype],
+                                   n, k, qptr, err.data_ptr(), stream.cuda_stream))
+    return err
+
+
+def tensor_error(blocks: torch.Tensor, ggml_type: int, x: torch.Tensor, qw: torch.Tensor | None = None) -> torch.Tensor:
+    """float64 device tensor [sum qw (decoded - x)^2, sum (decoded - x)^2] over the tensor,
+    summed in a fixed order (bit-identical across calls)."""
+    n, k, qptr = _error_args(blocks, ggml_type, x, qw)
+    out = torch.empty(2, dtype=torch.float64, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    with torch.cuda.device(x.device):
+        check(lib().qs_tensor_error(int(ggml_type), blocks.data_ptr(), blocks.stride(0), x.data_ptr(), SRC_IDS[x.dtype],
+                                    n, k, qptr, out.data_ptr(), stream.cuda_stream))
+    return out

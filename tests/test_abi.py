@@ -24,7 +24,8 @@ def declared_functions() -> list[str]:
 def test_header_declares_the_boundary():
     names = declared_functions()
     for n in ("qs_quantize", "qs_init", "qs_row_bytes", "qs_block_info", "qs_last_error",
-              "qs_type_supported", "qs_type_needs_qw", "qs_version"):
+              "qs_type_supported", "qs_type_needs_qw", "qs_version", "qs_dequantize", "qs_block_error",
+              "qs_tensor_error"):
         assert n in names
 
 
@@ -77,3 +78,21 @@ def test_argument_errors():
 def test_cpu_tensor_is_rejected_not_fallen_back():
     with pytest.raises(_native.QsError):
         _native.quantize(12, torch.zeros(2, 256), None)
+
+
+def test_decode_argument_errors():
+    """The decode entry points reject bad geometry before touching CUDA."""
+    L = _native.lib()
+    assert L.qs_dequantize(12, None, 144, 4, 250, None, 256, None) == _native.QS_EINVAL   # k % 256
+    assert L.qs_dequantize(12, None, 100, 4, 256, None, 256, None) == _native.QS_EINVAL   # row stride
+    assert L.qs_dequantize(12, None, 144, 4, 256, None, 255, None) == _native.QS_EINVAL   # dst stride
+    assert L.qs_dequantize(7, None, 144, 4, 256, None, 256, None) == _native.QS_ENOTSUP
+    assert L.qs_dequantize(12, None, 144, 0, 256, None, 256, None) == _native.QS_OK       # nothing to do
+    assert L.qs_block_error(12, None, 144, None, 5, 4, 256, None, None, None) == _native.QS_EINVAL
+    assert L.qs_block_error(12, None, 144, None, 30, 0, 256, None, None, None) == _native.QS_OK
+    assert L.qs_tensor_error(12, None, 144, None, 30, 4, 256, None, None, None) == _native.QS_EINVAL  # null out
+
+
+def test_cpu_blocks_are_rejected():
+    with pytest.raises(_native.QsError):
+        _native.dequantize(torch.zeros((2, 144), dtype=torch.uint8), 12)
