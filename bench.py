@@ -186,6 +186,9 @@ def main() -> None:
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="CPU seconds per reference step")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--op", default="quantize", choices=["quantize", "dequantize", "tensor_error"],
+                    help="quantize (the headline line); or time the block decode / the decode-error sum "
+                         "over the blocks of the same workload (HBM-bound, one GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -222,6 +225,9 @@ def main() -> None:
     outs = [torch.empty((x.shape[0], _native.row_bytes(gt, x.shape[1])), dtype=torch.uint8, device=device)
             for x in xs]
     stream = torch.cuda.Stream(device)
+    if args.op != "quantize":
+        bench_decode_op(torch, _native, gt, xs, qws, outs, stream, device, args, config, n_elem)
+        return
 
     def step(evs=None):
         for i, (x, q, o) in enumerate(zip(xs, qws, outs)):
@@ -310,6 +316,67 @@ def main() -> None:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def bench_decode_op(torch, _native, gt, xs, qws, outs, stream, device, args, config, n_elem):
+    """Time qs_dequantize or qs_tensor_error over the blocks of the workload (one GPU)."""
+    with torch.cuda.stream(stream):
+        for x, q, o in zip(xs, qws, outs):
+            _native.quantize_into(gt, x, q, o, stream)
+        if args.op == "dequantize":
+            fouts = [torch.empty(x.shape, dtype=torch.float32, device=device) for x in xs]
+            L = _native.lib()
+
+            def one(i):
+                _native.check(L.qs_dequantize(gt, outs[i].data_ptr(), outs[i].stride(0), xs[i].shape[0],
+                                              xs[i].shape[1], fouts[i].data_ptr(), fouts[i].stride(0),
+                                              stream.cuda_stream))
+            bytes_per_value = ALG_BYTES_OUT[args.qtype] + 4.0
+            launches_per_call = 1
+        else:
+            res = torch.empty(2, dtype=torch.float64, device=device)
+            L = _native.lib()
+
+            def one(i):
+                q = qws[i]
+                _native.check(L.qs_tensor_error(gt, outs[i].data_ptr(), outs[i].stride(0), xs[i].data_ptr(), 30,
+                                                xs[i].shape[0], xs[i].shape[1], None if q is None else q.data_ptr(),
+                                                res.data_ptr(), stream.cuda_stream))
+            bytes_per_value = ALG_BYTES_OUT[args.qtype] + 2.0
+            launches_per_call = 2
+        for _ in range(args.warmup):
+            for i in range(len(xs)):
+                one(i)
+    stream.synchronize()
+    kev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in xs]
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clk:
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for s in range(args.steps):
+            for i in range(len(xs)):
+                kev[s][i][0].record(stream)
+                one(i)
+                kev[s][i][1].record(stream)
+        t1.record(stream)
+        stream.synchronize()
+    ms_step = t0.elapsed_time(t1) / args.steps
+    launch_ms = statistics.mean(a.elapsed_time(b) for ev in kev for a, b in ev)
+    peaks = measured_peaks()
+    alg_bytes = n_elem / len(xs) * bytes_per_value
+    achieved = alg_bytes / (launch_ms * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None, "bytes_per_value": round(bytes_per_value, 4),
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"}
+    what = "packed blocks in + f32 values out" if args.op == "dequantize" else "packed blocks + bf16 rows in"
+    line = {"metric": f"{args.op} GB/s ({args.qtype}: {what})", "value": round(n_elem * bytes_per_value / (ms_step * 1e-3) / 1e9, 3),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32" if args.op == "dequantize" else "f64",
+            "data": "synthetic (blocks quantized on device from the seeded workload)",
+            "config": dict(config, op=args.op), "roofline": roof, "clocks": clk.summary(),
+            "gpu_launches": args.steps * len(xs) * launches_per_call, "kernel_ms_per_call": round(launch_ms, 4)}
+    print(json.dumps(line), flush=True)
 
 
 def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, world, n_elem):

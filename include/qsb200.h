@@ -102,9 +102,11 @@ int qs_dequantize(int ggml_type, const void* src, int64_t src_row_bytes, int64_t
                   float* dst, int64_t dst_row_stride, void* stream);
 
 /*
- * Squared error of every decoded block against the source values, in double:
+ * Squared error of every decoded block against the source values:
  *   err[r * (k / qk) + j] = sum over the values of block j of row r of w * (deq - x)^2,
- *   w = qw[column], or 1 when qw is NULL.
+ *   w = qw[column], or 1 when qw is NULL. Each term is a float32 product as the harness
+ *   computes it; each run of 8 consecutive values is summed left to right in float32,
+ *   and those partial sums in double.
  * The per-block form of the harness's decoded-error check (tools/dev_harness.py:110-112).
  *   blocks, blocks_row_bytes   as src / src_row_bytes of qs_dequantize
  *   x, x_type                  n_rows x k source values (F32 / F16 / BF16), rows
@@ -116,12 +118,13 @@ int qs_block_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, 
                    int64_t n_rows, int64_t k, const float* qw, double* err, void* stream);
 
 /*
- * Error sums over the whole tensor, in double and in a fixed order (the same bits on
- * every call on the same GPU model):
+ * Error sums over the whole tensor (terms and 8-value runs as qs_block_error), the runs
+ * added in double in a fixed order (the same bits on every call on the same GPU model):
  *   out[0] = sum w * (deq - x)^2, out[1] = sum (deq - x)^2   (out: 2 device doubles)
  * out[1] / (n_rows * k) is the `((dq - xf) ** 2).mean()` of tools/dev_harness.py:110-111.
  * Arguments as qs_block_error. Scratch for the per-CTA partial sums comes from the
- * stream-ordered allocator (cudaMallocAsync / cudaFreeAsync on `stream`).
+ * library's per-device memory pool, stream-ordered on `stream` (cudaMallocFromPoolAsync /
+ * cudaFreeAsync); the pool keeps its memory between calls.
  */
 int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x, int x_type,
                     int64_t n_rows, int64_t k, const float* qw, double* out, void* stream);

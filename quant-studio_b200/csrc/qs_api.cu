@@ -50,6 +50,7 @@ struct DeviceState {
     bool ready = false;
     int num_sms = 0;
     qs::IqTables* iq = nullptr;
+    cudaMemPool_t pool = nullptr;  // scratch of qs_tensor_error; keeps its memory between calls
 };
 
 std::mutex g_mu;
@@ -65,6 +66,15 @@ int ensure_device(int device, DeviceState** out) {
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
         e = qs::iq_tables_create(&d.iq);
         if (e != cudaSuccess) return cuda_fail(e, "uploading lattice tables");
+        cudaMemPoolProps props;
+        memset(&props, 0, sizeof(props));
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        if ((e = cudaMemPoolCreate(&d.pool, &props)) != cudaSuccess) return cuda_fail(e, "cudaMemPoolCreate");
+        uint64_t keep = UINT64_MAX;
+        if ((e = cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess)
+            return cuda_fail(e, "cudaMemPoolSetAttribute");
         d.ready = true;
     }
     *out = &d;
@@ -271,8 +281,8 @@ QS_API int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row
     const int np = qs::dq_partial_count(ggml_type, n_rows, k, ctx);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     void* partial = nullptr;
-    cudaError_t e = cudaMallocAsync(&partial, (size_t)np * 2 * sizeof(double), st);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync (partial sums)");
+    cudaError_t e = cudaMallocFromPoolAsync(&partial, (size_t)np * 2 * sizeof(double), d->pool, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync (partial sums)");
     e = qs::launch_tensor_error(ggml_type, c, static_cast<double*>(partial), np, out, ctx, d->iq);
     cudaError_t ef = cudaFreeAsync(partial, st);
     if (e != cudaSuccess) return cuda_fail(e, "tensor error launch");

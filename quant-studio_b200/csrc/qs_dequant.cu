@@ -7,7 +7,8 @@
 // float32 operations in the same order, so the values are bit-identical. The checkers
 // measure what that harness measures next (tools/dev_harness.py:110-112), the squared
 // error of the decoded values against the source rows, with optional importance
-// weights, accumulated in double.
+// weights: per value in float32 like the harness, (deq - x)^2 and w * (deq - x)^2;
+// 8 consecutive values summed left to right in float32; everything above in double.
 //
 // Mapping: a CTA of 256 threads takes a tile of blocks (8 superblocks, or 64 Q4_0
 // blocks), copies their bytes to shared memory with 16-byte loads, and each thread
@@ -259,11 +260,15 @@ struct DqArgs {
 
 __device__ __forceinline__ void load_x8(const void* base, int64_t e0, int src, float* v) { load_row<8>(base, e0, src, v); }
 
+// resident CTAs per SM the register budget is sized for: the decode keeps little live
+// across the staging; the checkers hold the prefetched source values and weights
+template <int MODE> struct DqOcc { static constexpr int CTAS = MODE == DQ_DECODE ? 5 : 4; };
+
 template <int TYPE, int MODE>
-__global__ void __launch_bounds__(DQ_THREADS) dq_kernel(DqArgs a) {
+__global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArgs a) {
     using D = Dq<TYPE>;
     constexpr int TPB = D::QK / 8, BPT = DQ_THREADS / TPB;  // threads per block, blocks per tile
-    __shared__ __align__(16) uint8_t s_blk[BPT * D::BB + 16];
+    __shared__ __align__(16) uint8_t s_blk[BPT * D::BB + 32];
     __shared__ double s_red[2][DQ_THREADS / 32];
     const int tid = threadIdx.x, lb = tid / TPB, t = tid % TPB;
     const bool packed = a.src_row_bytes == a.nblk_row * D::BB;
@@ -272,51 +277,60 @@ __global__ void __launch_bounds__(DQ_THREADS) dq_kernel(DqArgs a) {
     for (int64_t tile = blockIdx.x; tile * BPT < a.nblk; tile += gridDim.x) {
         const int64_t b0 = tile * BPT;
         const int nb = (int)min((int64_t)BPT, a.nblk - b0);
+        const bool live = lb < nb;
+        const int64_t b = b0 + lb;
+        // the source values and weights do not depend on the blocks: in flight with the staging
+        float xv[8], w[8];
+        if (MODE != DQ_DECODE && live) {
+            const int64_t row = b / a.nblk_row, col = (b - row * a.nblk_row) * D::QK + 8 * t;
+            load_x8(a.x, row * a.k + col, a.x_type, xv);
+            if (a.qw) load_f32<8>(a.qw + col, w);
+        }
+        const uint8_t* tb;
         if (packed) {
-            // the tile is one contiguous span of nb * BB bytes
+            // one contiguous span of nb * BB bytes, placed at s_blk + (address & 15) so the
+            // 16-byte aligned body moves with 16-byte loads and stores
             const uint8_t* g = a.src + b0 * D::BB;
-            const int nbytes = nb * D::BB;
-            const int head = (int)((16 - ((uintptr_t)g & 15)) & 15) < nbytes ? (int)((16 - ((uintptr_t)g & 15)) & 15) : nbytes;
-            for (int i = tid; i < head; i += DQ_THREADS) s_blk[i] = __ldg(g + i);
-            const int body = (nbytes - head) / 16;
+            const int mis = (int)((uintptr_t)g & 15), nbytes = nb * D::BB;
+            const int head = min((16 - mis) & 15, nbytes), body = (nbytes - head) / 16;
+            uint8_t* sp = s_blk + mis;
+            for (int i = tid; i < head; i += DQ_THREADS) sp[i] = __ldg(g + i);
             const uint4* g4 = reinterpret_cast<const uint4*>(g + head);
-            for (int i = tid; i < body; i += DQ_THREADS) {
-                const uint4 w = __ldg(g4 + i);
-                uint8_t* s = s_blk + head + 16 * i;
-                const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int j = 0; j < 16; j++) s[j] = (uint8_t)(w4[j >> 2] >> (8 * (j & 3)));
-            }
-            for (int i = head + 16 * body + tid; i < nbytes; i += DQ_THREADS) s_blk[i] = __ldg(g + i);
+            uint4* s4 = reinterpret_cast<uint4*>(sp + head);
+            for (int i = tid; i < body; i += DQ_THREADS) s4[i] = __ldg(g4 + i);
+            for (int i = head + 16 * body + tid; i < nbytes; i += DQ_THREADS) sp[i] = __ldg(g + i);
+            tb = sp;
         } else {
             for (int i = tid; i < nb * D::BB; i += DQ_THREADS) {
                 const int64_t bb = b0 + i / D::BB;
-                const int64_t row = bb / a.nblk_row, col = bb - row * a.nblk_row;
-                s_blk[i] = __ldg(a.src + row * a.src_row_bytes + col * D::BB + i % D::BB);
+                const int64_t r = bb / a.nblk_row, c = bb - r * a.nblk_row;
+                s_blk[i] = __ldg(a.src + r * a.src_row_bytes + c * D::BB + i % D::BB);
             }
+            tb = s_blk;
         }
         __syncthreads();
-        if (lb < nb) {
+        if (live) {
             float v[8];
-            D::decode(s_blk + lb * D::BB, t, a.kgrid, v);
-            const int64_t b = b0 + lb, row = b / a.nblk_row;
-            const int64_t col = (b - row * a.nblk_row) * D::QK + 8 * t;
+            D::decode(tb + lb * D::BB, t, a.kgrid, v);
             if (MODE == DQ_DECODE) {
+                const int64_t row = b / a.nblk_row, col = (b - row * a.nblk_row) * D::QK + 8 * t;
                 float4* o = reinterpret_cast<float4*>(a.dst + row * a.dst_stride + col);
                 o[0] = make_float4(v[0], v[1], v[2], v[3]);
                 o[1] = make_float4(v[4], v[5], v[6], v[7]);
             } else {
-                float xv[8], w[8];
-                load_x8(a.x, row * a.k + col, a.x_type, xv);
-                if (a.qw) load_f32<8>(a.qw + col, w);
-                double ew = 0.0, e2 = 0.0;
+                // per value in float32 as the reference harness computes it, (deq - x)^2
+                // and w * that; the 8 values summed left to right in float32, then double
+                float fw = 0.0f, f2 = 0.0f;
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const double e = (double)v[i] - (double)xv[i];
-                    const double ee = e * e;
-                    e2 += ee;
-                    ew += a.qw ? (double)w[i] * ee : ee;
+                    const float e = v[i] - xv[i];
+                    const float ee = e * e;
+                    const float we = a.qw ? w[i] * ee : ee;
+                    f2 = i == 0 ? ee : f2 + ee;
+                    fw = i == 0 ? we : fw + we;
                 }
+                double ew = (double)fw;
+                const double e2 = (double)f2;
                 if (MODE == DQ_BLOCK_ERR) {
                     // the TPB threads of the block are adjacent lanes; fixed xor tree
 #pragma unroll

@@ -3,9 +3,9 @@
 Decode parity: every value bit-identical to gguf-py's gguf.quants.dequantize (the
 decode of the reference's correctness harness, tools/dev_harness.py:108-109) on the
 golden fixture blocks and on random blocks of every format. Error checkers: per-block
-and whole-tensor sums of qw * (deq - x)^2 against the same sums in numpy float64
-(relative 1e-12: only the association of the double additions differs), and the
-tensor sums bit-identical from call to call.
+and whole-tensor sums of qw * (deq - x)^2 against the same definition restated in numpy
+(float32 terms and runs of 8, double above; relative 1e-12 since only the association
+of the double additions differs), and the tensor sums bit-identical from call to call.
 """
 
 import numpy as np
@@ -84,12 +84,23 @@ def test_decode_empty_and_errors():
         nat.dequantize(torch.zeros((2, 145), dtype=torch.uint8, device="cuda"), 12)
 
 
+def _runs8(t: np.ndarray) -> np.ndarray:
+    """float32 sums of each run of 8 consecutive values, left to right, as float64."""
+    t = t.reshape(t.shape[0], -1, 8)
+    s = t[..., 0].copy()
+    for j in range(1, 8):
+        s = s + t[..., j]
+    return s.astype(np.float64)
+
+
 def _ref_errors(deq: np.ndarray, x: np.ndarray, qw, qk: int):
-    e = deq.astype(np.float64) - x.astype(np.float64)
+    """The checkers' definition: float32 terms, float32 runs of 8, double above."""
+    e = deq.astype(np.float32) - x.astype(np.float32)
     ee = e * e
-    w = np.ones(x.shape[1]) if qw is None else qw.astype(np.float64)
-    blk = (ee * w[None, :]).reshape(x.shape[0], -1, qk).sum(-1)
-    return blk, (ee * w[None, :]).sum(), ee.sum()
+    we = ee if qw is None else qw.astype(np.float32)[None, :] * ee
+    rw, r = _runs8(we), _runs8(ee)
+    blk = rw.reshape(x.shape[0], -1, qk // 8).sum(-1)
+    return blk, rw.sum(), r.sum()
 
 
 @pytest.mark.parametrize("qtype", ALL_TYPES)
@@ -125,10 +136,9 @@ def test_tensor_error_large_ragged():
     x = (torch.randn((3001, 2048), device="cuda", generator=g) * 0.02).to(torch.bfloat16)
     qw = torch.rand(2048, device="cuda", generator=g) + 0.1
     blocks = nat.quantize(12, x, qw)
-    deq = nat.dequantize(blocks, 12)
-    e = deq.double() - x.double()
-    want = torch.stack([(e * e * qw.double()).sum(), (e * e).sum()]).cpu().numpy()
+    deq = nat.dequantize(blocks, 12).cpu().numpy()
+    _, want_w, want = _ref_errors(deq, x.float().cpu().numpy(), qw.cpu().numpy(), 256)
     got = nat.tensor_error(blocks, 12, x, qw).cpu().numpy()
-    np.testing.assert_allclose(got, want, rtol=1e-10, atol=0)
+    np.testing.assert_allclose(got, [want_w, want], rtol=1e-10, atol=0)
     blk = nat.block_error(blocks, 12, x, qw)
-    np.testing.assert_allclose(blk.sum().item(), want[0], rtol=1e-10)
+    np.testing.assert_allclose(blk.sum().item(), want_w, rtol=1e-10)
