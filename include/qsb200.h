@@ -129,6 +129,30 @@ int qs_block_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, 
 int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x, int x_type,
                     int64_t n_rows, int64_t k, const float* qw, double* out, void* stream);
 
+/* Capacity of the static scratch of qs_tensor_error_noalloc, in per-CTA partial sums. */
+#define QS_NOALLOC_MAX_PARTIALS 4096
+
+/*
+ * qs_tensor_error without any allocation. No counterpart in the reference (its harness
+ * sums the decoded error on the host, tools/dev_harness.py:110-111); an addition of this
+ * library for callers that may not allocate device memory.
+ * Same arguments, same kernels and the same result bits as qs_tensor_error, but the
+ * per-CTA partial sums live in a fixed static device array of QS_NOALLOC_MAX_PARTIALS
+ * pairs of doubles (64 KiB per device) and the IQ codebooks in a 5 KiB static device
+ * array: no cudaMalloc, no pool, no library allocator on any call. The launch uses one
+ * partial sum per CTA, at most 8 CTAs per SM; a launch that would need more than
+ * QS_NOALLOC_MAX_PARTIALS (a GPU with more than 512 SMs) is rejected with QS_EINVAL before
+ * anything is enqueued. Nothing in the static scratch needs to start at zero: each CTA
+ * writes its own pair before the final pass reads them.
+ * Overlapping calls on one device (concurrent streams or host threads) share the static
+ * scratch and race; callers must serialize them.
+ * Set-up: the first call on each device, with that device current, resolves the static
+ * arrays (cudaGetSymbolAddress) and copies the codebooks in (a synchronous copy); make
+ * that first call outside any stream capture.
+ */
+int qs_tensor_error_noalloc(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x,
+                            int x_type, int64_t n_rows, int64_t k, const float* qw, double* out, void* stream);
+
 /* Message of the calling thread's last failure ("" if none). */
 const char* qs_last_error(void);
 

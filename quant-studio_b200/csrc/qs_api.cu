@@ -289,4 +289,38 @@ QS_API int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row
     return ef == cudaSuccess ? QS_OK : cuda_fail(ef, "cudaFreeAsync (partial sums)");
 }
 
+static_assert(qs::NA_MAX_PARTIALS == QS_NOALLOC_MAX_PARTIALS, "static scratch size and its public constant differ");
+
+QS_API int qs_tensor_error_noalloc(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x,
+                                   int x_type, int64_t n_rows, int64_t k, const float* qw, double* out, void* stream) {
+    // allocation-free: no ensure_device (it uploads tables and creates a pool), only the
+    // static scratch resolved by noalloc_setup
+    qs::DqCall c;
+    int rc = check_decode(ggml_type, blocks, blocks_row_bytes, n_rows, k, c);
+    if (rc) return rc;
+    if (!out) return fail(QS_EINVAL, "null out");
+    if (n_rows > 0) {
+        if ((rc = check_source(x, x_type, qw))) return rc;
+        if (!blocks) return fail(QS_EINVAL, "null blocks");
+    }
+    cudaPointerAttributes pa;
+    cudaError_t e = cudaPointerGetAttributes(&pa, out);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+    if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) return fail(QS_EINVAL, "out is not device memory");
+    int cur = -1;
+    if ((e = cudaGetDevice(&cur)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur != pa.device && (e = cudaSetDevice(pa.device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    const qs::NoAllocDevice* d = nullptr;
+    if ((e = qs::noalloc_setup(pa.device, &d)) != cudaSuccess) return cuda_fail(e, "static scratch set-up");
+    c.x = x;
+    c.x_type = x_type;
+    c.qw = qw;
+    qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), pa.device, d->num_sms};
+    const int need = qs::dq_partial_count(ggml_type, n_rows, k, ctx);
+    if (need > QS_NOALLOC_MAX_PARTIALS)
+        return fail(QS_EINVAL, "launch needs %d partial sums; the static scratch holds %d", need, QS_NOALLOC_MAX_PARTIALS);
+    e = qs::launch_tensor_error_noalloc(ggml_type, c, out, ctx, *d);
+    return e == cudaSuccess ? QS_OK : cuda_fail(e, "tensor error launch (static scratch)");
+}
+
 }  // extern "C"

@@ -14,6 +14,9 @@
 // blocks), copies their bytes to shared memory with 16-byte loads, and each thread
 // decodes 8 consecutive values of one block. HBM-bound: the decode writes 4 bytes per
 // value, the checkers read the source rows (2 or 4 bytes per value).
+#include <mutex>
+
+#include "iq_grids.h"
 #include "qs_kernels.h"
 
 namespace qs {
@@ -461,6 +464,73 @@ cudaError_t launch_tensor_error(int type, const DqCall& c, double* partial, int 
     cudaError_t e = a.nblk ? launch_dq_mode<DQ_SUM_ERR>(type, a, ctx, grid) : cudaSuccess;
     if (e != cudaSuccess) return e;
     dq_finish_kernel<<<1, DQ_THREADS, 0, ctx.stream>>>(partial, a.nblk ? grid : 0, out);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// qs_tensor_error_noalloc: the same launch with its scratch in static device memory
+// ---------------------------------------------------------------------------
+namespace {
+
+// Per-CTA partial sums (weighted, plain) of one launch. Every CTA of the launch writes its
+// own pair before the final pass reads the pairs, so nothing here needs to start at zero.
+__device__ __align__(256) double g_na_partial[2 * NA_MAX_PARTIALS];
+// The five IQ codebooks (grid index -> code), copied in once per device at set-up.
+constexpr int NA_KG_OFF[5] = {0, 256, 768, 1792, 2048};
+__device__ __align__(256) uint16_t g_na_kgrid[256 + 512 + 1024 + 256 + 512];
+
+std::mutex g_na_mu;
+NoAllocDevice g_na_dev[NA_MAX_DEVICES];
+
+}  // namespace
+
+cudaError_t noalloc_setup(int device, const NoAllocDevice** out) {
+    if (device < 0 || device >= NA_MAX_DEVICES) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(g_na_mu);
+    NoAllocDevice& d = g_na_dev[device];
+    if (!d.ready) {
+        cudaError_t e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) return e;
+        void* p = nullptr;
+        if ((e = cudaGetSymbolAddress(&p, g_na_partial)) != cudaSuccess) return e;
+        d.partial = static_cast<double*>(p);
+        if ((e = cudaGetSymbolAddress(&p, g_na_kgrid)) != cudaSuccess) return e;
+        uint16_t* kg = static_cast<uint16_t*>(p);
+        const uint16_t* src[5] = {KGRID_2BIT_256, KGRID_2BIT_512, KGRID_2BIT_1024, KGRID_3BIT_256, KGRID_3BIT_512};
+        const int n[5] = {256, 512, 1024, 256, 512};
+        for (int i = 0; i < 5; i++)
+            if ((e = cudaMemcpy(kg + NA_KG_OFF[i], src[i], n[i] * sizeof(uint16_t), cudaMemcpyHostToDevice)) != cudaSuccess)
+                return e;
+        d.kgrid = kg;
+        d.ready = true;
+    }
+    *out = &d;
+    return cudaSuccess;
+}
+
+cudaError_t launch_tensor_error_noalloc(int type, const DqCall& c, double* out, const LaunchCtx& ctx,
+                                        const NoAllocDevice& d) {
+    DqArgs a;
+    a.src = static_cast<const uint8_t*>(c.blocks);
+    a.src_row_bytes = c.blocks_row_bytes;
+    a.n_rows = c.n_rows;
+    a.k = c.k;
+    a.nblk_row = c.k / block_qk(type);
+    a.nblk = c.n_rows * a.nblk_row;
+    a.dst = nullptr;
+    a.dst_stride = 0;
+    a.x = c.x;
+    a.x_type = c.x_type;
+    a.qw = c.qw;
+    a.err = nullptr;
+    a.partial = d.partial;
+    const int gi = type == QS_IQ2_XXS ? 0 : type == QS_IQ2_XS ? 1 : type == QS_IQ2_S ? 2 : type == QS_IQ3_XXS ? 3 : 4;
+    a.kgrid = d.kgrid + NA_KG_OFF[gi];
+    const int grid = dq_grid(type, a.nblk, ctx);
+    if (grid > NA_MAX_PARTIALS) return cudaErrorInvalidValue;
+    cudaError_t e = a.nblk ? launch_dq_mode<DQ_SUM_ERR>(type, a, ctx, grid) : cudaSuccess;
+    if (e != cudaSuccess) return e;
+    dq_finish_kernel<<<1, DQ_THREADS, 0, ctx.stream>>>(d.partial, a.nblk ? grid : 0, out);
     return cudaGetLastError();
 }
 

@@ -60,4 +60,21 @@ int dq_partial_count(int type, int64_t n_rows, int64_t k, const LaunchCtx& ctx);
 cudaError_t launch_tensor_error(int type, const DqCall& c, double* partial, int npartial, double* out,
                                 const LaunchCtx& ctx, const IqTables* t);
 
+// qs_tensor_error_noalloc: static device scratch resolved once per device (qs_dequant.cu).
+constexpr int NA_MAX_PARTIALS = 4096;  // pairs of doubles: 64 KiB per device
+constexpr int NA_MAX_DEVICES = 64;
+struct NoAllocDevice {
+    bool ready = false;
+    int num_sms = 0;
+    double* partial = nullptr;        // device address of the static partial sums
+    const uint16_t* kgrid = nullptr;  // device address of the static codebooks
+};
+// With `device` current: resolve the static arrays (cudaGetSymbolAddress) and fill the
+// codebooks, once per device; thread-safe.
+cudaError_t noalloc_setup(int device, const NoAllocDevice** out);
+// qs_tensor_error's launch on the static scratch; cudaErrorInvalidValue if the launch
+// needs more than NA_MAX_PARTIALS partial sums (nothing is launched then).
+cudaError_t launch_tensor_error_noalloc(int type, const DqCall& c, double* out, const LaunchCtx& ctx,
+                                        const NoAllocDevice& d);
+
 }  // namespace qs
