@@ -17,7 +17,14 @@ namespace qs {
 // ahead of the one being quantized, so memory stays busy without holding the data in
 // registers. Each lane then quantizes one whole block: no shuffles, one reciprocal per
 // block. d = max / -8 is computed as max * -0.125 (the same IEEE value).
+// In the ring, 16-byte chunk i of block b sits at slot CPB * b + (i ^ swz(b)) (CPB = 4 or
+// 8 chunks per block): the 8 lanes of a quarter warp then read 8 distinct 16-byte bank
+// groups when each loads chunk i of its own block.
 // ---------------------------------------------------------------------------
+template <int CPB>
+__device__ __forceinline__ int q40_slot(int b, int i) {
+    return CPB * b + (i ^ (CPB == 4 ? ((b >> 1) & 3) : (b & 7)));
+}
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
@@ -37,12 +44,15 @@ __global__ void __launch_bounds__(256, 3) q4_0_kernel(QuantArgs a) {
     const int64_t ntile = (a.nblk + 31) / 32, lim = a.nblk * 32 * ES;
     const int64_t stride = (int64_t)gridDim.x * WARPS;
     const int64_t t_first = (int64_t)blockIdx.x * WARPS + warp;
+    constexpr int CPB = 2 * ES;  // 16-byte chunks per 32-value block
     auto issue = [&](int64_t t, int stage) {  // one commit group per tile, empty past the end
         if (t < ntile) {
 #pragma unroll
             for (int j = 0; j < NV; j++) {
                 const int64_t off = t * TILE + 512 * j + 16 * lane;
-                cp_async16(ring + stage * TILE + 512 * j + 16 * lane, off < lim ? src + off : src, off < lim ? 16 : 0);
+                const int g = 32 * j + lane;  // chunk of the tile
+                cp_async16(ring + stage * TILE + 16 * q40_slot<CPB>(g / CPB, g % CPB), off < lim ? src + off : src,
+                           off < lim ? 16 : 0);
             }
         }
         cp_async_commit();
@@ -56,11 +66,11 @@ __global__ void __launch_bounds__(256, 3) q4_0_kernel(QuantArgs a) {
         __syncwarp();                 // ... and every other lane's
         const int nvalid = (int)min((int64_t)32, a.nblk - tile * 32);
         float x[32], mx, mn;
-        const uint8_t* blk = ring + stage * TILE + lane * 32 * ES;
+        const uint4* blk = reinterpret_cast<const uint4*>(ring + stage * TILE);
         if (ES == 4) {
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                const float4 f = reinterpret_cast<const float4*>(blk)[i];
+                const float4 f = reinterpret_cast<const float4*>(blk)[q40_slot<CPB>(lane, i)];
                 x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
             }
             mx = x[0];
@@ -72,7 +82,7 @@ __global__ void __launch_bounds__(256, 3) q4_0_kernel(QuantArgs a) {
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const uint4 t = reinterpret_cast<const uint4*>(blk)[i];
+                const uint4 t = blk[q40_slot<CPB>(lane, i)];
                 w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
             }
             if (a.src_type == SRC_BF16) {
@@ -141,7 +151,15 @@ __global__ void __launch_bounds__(256, 3) q4_0_kernel(QuantArgs a) {
             for (int i = 0; i < 4; i++) { o16[1 + 2 * i] = (uint16_t)wq[i]; o16[2 + 2 * i] = (uint16_t)(wq[i] >> 16); }
         }
         __syncwarp();
-        store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
+        if (nvalid == 32 && a.dst_row_bytes == a.row_bytes && (((uintptr_t)a.dst & 15) == 0)) {
+            // whole tile, contiguous rows: 576 bytes = 36 aligned 16-byte chunks
+            uint4* d4 = reinterpret_cast<uint4*>(a.dst + tile * 32 * BB);
+            const uint4* s4 = reinterpret_cast<const uint4*>(so);
+            d4[lane] = s4[lane];
+            if (lane < 4) d4[32 + lane] = s4[32 + lane];
+        } else {
+            store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
+        }
         __syncwarp();  // the stage and the output staging are free again
         stage = (stage + 1) % STAGES;
     }
