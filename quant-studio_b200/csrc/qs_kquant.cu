@@ -444,22 +444,26 @@ __global__ void __launch_bounds__(256) qx_kernel(QuantArgs a, KParams p) {
         s_ls[sbl][g] = (float)myls;
         __syncwarp();
 
+        // the group's 16 level bytes go to shared memory as one 16-byte store (lanes at a
+        // 16-byte stride: no bank conflicts)
         const float dd = f16_val(d16);
+        uint32_t pk[4] = {0u, 0u, 0u, 0u};
         if (T == QS_Q6_K) {
             const float dq = dd * (float)myls;
 #pragma unroll
             for (int i = 0; i < GS; i++) {
                 const float v = dq != 0.0f ? clampf(rintf(__fdiv_rn(x[i], dq)), -32.0f, 31.0f) + 32.0f : L[i];
-                lev[g * GS + i] = live ? (uint8_t)(int)v : 0;
+                pk[i >> 2] |= (live ? (uint32_t)(int)v & 0xFFu : 0u) << (8 * (i & 3));
             }
         } else {
             const float dq = dd * (float)(myls - 32);
 #pragma unroll
             for (int i = 0; i < GS; i++) {
                 const float v = dq != 0.0f ? clampf(rintf(__fdiv_rn(x[i], dq)), -4.0f, 3.0f) + 4.0f : L[i];
-                lev[g * GS + i] = (uint8_t)(int)v;
+                pk[i >> 2] |= ((uint32_t)(int)v & 0xFFu) << (8 * (i & 3));
             }
         }
+        *reinterpret_cast<uint4*>(lev + g * GS) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         __syncwarp();
 
         uint8_t* o = s_out + sbl * BB;
