@@ -186,10 +186,18 @@ def main() -> None:
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="CPU seconds per reference step")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
-    ap.add_argument("--op", default="quantize", choices=["quantize", "dequantize", "tensor_error"],
+    ap.add_argument("--op", default="quantize", choices=["quantize", "dequantize", "tensor_error", "cli"],
                     help="quantize (the headline line); or time the block decode / the decode-error sum "
-                         "over the blocks of the same workload (HBM-bound, one GPU)")
+                         "over the blocks of the same workload (HBM-bound, one GPU); or `cli`: the drop-in "
+                         "CLI on a whole synthetic model (BASELINE configs 4 / 5), sharded over --gpus")
+    ap.add_argument("--model", default="4b", choices=["4b", "8b"], help="--op cli: synthetic model class")
+    ap.add_argument("--scheme", default=None, help="--op cli: scheme (default Q4_K_M for 4b, IQ3_XXS for 8b)")
+    ap.add_argument("--model-dir", default=None, help="--op cli: directory for the synthetic model and output")
+    ap.add_argument("--mem", default="4G", help="--op cli: the CLI's --mem")
     args = ap.parse_args()
+    if args.op == "cli":
+        bench_cli(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     rank = int(os.environ.get("RANK", "0"))
@@ -376,6 +384,57 @@ def bench_decode_op(torch, _native, gt, xs, qws, outs, stream, device, args, con
             "data": "synthetic (blocks quantized on device from the seeded workload)",
             "config": dict(config, op=args.op), "roofline": roof, "clocks": clk.summary(),
             "gpu_launches": args.steps * len(xs) * launches_per_call, "kernel_ms_per_call": round(launch_ms, 4)}
+    print(json.dumps(line), flush=True)
+
+
+def bench_cli(args) -> None:
+    """Whole-model quantization through the drop-in CLI (quant-studio.py) on a synthetic
+    bf16 model of BASELINE's config 4 (4B-class, Q4_K_M + imatrix) or 5 (8B-class, IQ3_XXS /
+    IQ2_M + imatrix): one process, row chunks sharded over --gpus, blocks written with pwrite.
+    value = bf16 tensor bytes / the CLI's quantization time (reading the mapped model, copies,
+    kernels, copies back, writes); the CLI's process wall time (startup, planning, fsync) is
+    reported beside it. --warmup runs are untimed (page cache, CUDA start-up)."""
+    import re
+    import tempfile
+
+    sys.path.insert(0, str(ROOT / "quant-studio_b200"))
+    import synth_model
+
+    scheme = args.scheme or ("Q4_K_M" if args.model == "4b" else "IQ3_XXS")
+    d = Path(args.model_dir or Path(tempfile.gettempdir()) / "qsb200_synth")
+    d.mkdir(parents=True, exist_ok=True)
+    model, imat = d / f"synth-{args.model}.gguf", d / f"synth-{args.model}.imatrix.gguf"
+    gen_s = None
+    if not (model.exists() and imat.exists()):
+        t0 = time.time()
+        cols = synth_model.write_model(model, args.model)
+        synth_model.write_imatrix(imat, cols)
+        gen_s = round(time.time() - t0, 2)
+    cfg = synth_model.MODELS[args.model]
+    n_w = sum(r * c for _, (r, c), w in ((n, s, w) for n, s, w in synth_model.tensor_list(cfg) if w))
+    out = d / f"out-{args.model}-{scheme}.gguf"
+    cmd = [sys.executable, str(ROOT / "quant-studio_b200" / "quant-studio.py"), str(model), str(out), scheme,
+           "--imatrix", str(imat), "--gpus", str(args.gpus), "--mem", args.mem]
+    runs = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.time()
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        wall = time.time() - t0
+        if r.returncode != 0:
+            raise SystemExit(f"CLI failed ({r.returncode}): {r.stderr[-2000:]}")
+        m = re.search(r"done in ([0-9.]+)s", r.stdout)
+        if i >= args.warmup:
+            runs.append((float(m.group(1)), wall))
+    q_s = statistics.median(x for x, _ in runs)
+    wall_s = statistics.median(y for _, y in runs)
+    line = {"metric": f"CLI input GB/s (synthetic {args.model.upper()}-class bf16 GGUF -> {scheme}, imatrix)",
+            "value": round(2 * n_w / q_s / 1e9, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(q_s * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16 in", "data": "synthetic (BASELINE config architecture, random-init weights)",
+            "config": {"workload": f"BASELINE configs[{3 if args.model == '4b' else 4}]: {args.model} model, {scheme} + imatrix, "
+                                   f"--gpus {args.gpus}, --mem {args.mem}", "weight_values": n_w,
+                       "model_bytes": model.stat().st_size, "output_bytes": out.stat().st_size},
+            "quantize_s": round(q_s, 3), "cli_wall_s": round(wall_s, 2), "generate_s": gen_s}
     print(json.dumps(line), flush=True)
 
 

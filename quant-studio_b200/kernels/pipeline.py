@@ -13,6 +13,9 @@ every tensor an aligned offset), so any chunk can be written the moment it is re
     (no f32 upcast), copies the blocks back and writes them with os.pwrite;
   * two slots per GPU, each with its own stream, so the host copy and the file write of
     one chunk overlap the device work of the other;
+  * the copy of a chunk from the mapped model into pinned memory is split over a shared
+    pool of host threads (numpy releases the GIL for it): one thread moves only a few GB/s
+    and takes the mapping's page faults alone, which made it the bottleneck of the CLI;
   * passthrough tensors are copied with pwrite from the source mmap.
 No collective and no peer traffic: the GPUs share nothing but the queue.
 """
@@ -23,6 +26,7 @@ import os
 import queue
 import threading
 import time
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 
 import numpy as np
@@ -58,6 +62,7 @@ class _Slot:
         self.h_in = self.h_out = None
         self.d_in = self.d_out = None
         self.pending = None       # (nbytes, file offset) of the chunk in flight
+        self.qw = None            # the weights the chunk in flight reads: kept alive until it is retired
 
     @staticmethod
     def _grow_pinned(buf, nbytes):
@@ -75,12 +80,27 @@ class _Slot:
 class ShardedQuantizer:
     """Quantize a list of jobs across `devices`, writing into the open file `fd`."""
 
-    def __init__(self, devices: list[torch.device], fd: int, mem_bytes: int):
+    COPY_SLICE = 8 << 20  # bytes per host-copy task
+
+    def __init__(self, devices: list[torch.device], fd: int, mem_bytes: int, copy_threads: int | None = None):
         self.devices = devices
         self.fd = fd
         self.mem_bytes = mem_bytes
         self.error: BaseException | None = None
         self.stats: dict[str, float] = {}
+        self.copy_threads = copy_threads or min(32, os.cpu_count() or 1)
+        self._pool: ThreadPoolExecutor | None = None
+
+    def _copy_rows(self, dst: np.ndarray, src: np.ndarray) -> None:
+        """dst[:] = src for (n, row_bytes) arrays, in row slices on the copy pool."""
+        n = src.shape[0]
+        per = max(1, self.COPY_SLICE // max(1, src.shape[1]))
+        if self._pool is None or n <= per:
+            np.copyto(dst, src)
+            return
+        futs = [self._pool.submit(np.copyto, dst[r:r + per], src[r:r + per]) for r in range(0, n, per)]
+        for f in futs:
+            f.result()
 
     # -- work list ---------------------------------------------------------
     def _chunks(self, jobs: list[QuantJob]):
@@ -108,7 +128,7 @@ class ShardedQuantizer:
         slot.h_out = _Slot._grow_pinned(slot.h_out, out_bytes)
         slot.d_in = _Slot._grow_dev(slot.d_in, in_bytes, device)
         slot.d_out = _Slot._grow_dev(slot.d_out, out_bytes, device)
-        np.copyto(slot.h_in[:in_bytes].numpy().reshape(n, -1), job.rows[r0:r1])
+        self._copy_rows(slot.h_in[:in_bytes].numpy().reshape(n, -1), job.rows[r0:r1])
         qw = None
         if job.qw is not None:
             cache = ctx["qw"]
@@ -116,6 +136,9 @@ class ShardedQuantizer:
                 cache.clear()
                 cache[id(job)] = torch.from_numpy(np.ascontiguousarray(job.qw[:job.k], dtype=np.float32)).to(device)
             qw = cache[id(job)]
+        # the other slot's kernel may still read the previous job's weights; holding them here
+        # keeps the caching allocator from giving their memory to the next upload
+        slot.qw = qw
         with torch.cuda.stream(slot.stream):
             if qw is not None:
                 slot.stream.wait_stream(torch.cuda.current_stream(device))
@@ -137,6 +160,7 @@ class ShardedQuantizer:
             return
         nbytes, off = slot.pending
         slot.event.synchronize()
+        slot.qw = None
         self._write(slot.h_out[:nbytes].numpy(), off)
         slot.pending = None
 
@@ -170,13 +194,19 @@ class ShardedQuantizer:
         for _ in self.devices:
             work.put(None)
         lock = threading.Lock()
-        threads = [threading.Thread(target=self._worker, args=(d, work, lock), daemon=True) for d in self.devices]
-        for t in threads:
-            t.start()
-        for c in copies:  # passthroughs on this thread while the GPUs work
-            self._write(np.ascontiguousarray(c.data), c.out_offset)
-        for t in threads:
-            t.join()
+        self._pool = ThreadPoolExecutor(max_workers=self.copy_threads) if self.copy_threads > 1 else None
+        try:
+            threads = [threading.Thread(target=self._worker, args=(d, work, lock), daemon=True) for d in self.devices]
+            for t in threads:
+                t.start()
+            for c in copies:  # passthroughs on this thread while the GPUs work
+                self._write(np.ascontiguousarray(c.data), c.out_offset)
+            for t in threads:
+                t.join()
+        finally:
+            if self._pool is not None:
+                self._pool.shutdown(wait=True)
+                self._pool = None
         if self.error is not None:
             raise self.error
         return time.time() - t0

@@ -288,7 +288,7 @@ def main() -> None:
               f"{dst.name if dst else t.tensor_type.name:<8s} {fmt_size(t.n_bytes)} -> {fmt_size(nb)}")
     os.fsync(fd)
     writer.close()
-    print(f"done in {dt:.1f}s: {fmt_size(tin)} -> {fmt_size(tout)} ({tout / max(tin, 1) * 100:.1f}%)")
+    print(f"done in {dt:.3f}s: {fmt_size(tin)} -> {fmt_size(tout)} ({tout / max(tin, 1) * 100:.1f}%)")
 
 
 if __name__ == "__main__":

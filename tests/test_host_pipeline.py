@@ -101,3 +101,20 @@ def test_max_over_ranks_gloo():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: 11.0, 1: 11.0}
+
+
+def test_host_copy_split_over_the_pool():
+    """A chunk larger than one copy slice is copied in row slices on the pool, exactly."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from kernels.pipeline import ShardedQuantizer
+
+    sq = ShardedQuantizer([], fd=-1, mem_bytes=1 << 30, copy_threads=4)
+    src = np.random.default_rng(0).integers(0, 256, size=(3001, 8192), dtype=np.uint8)  # 24.6 MB, 4 slices
+    dst = np.zeros_like(src)
+    sq._pool = ThreadPoolExecutor(max_workers=4)
+    try:
+        sq._copy_rows(dst, src)
+    finally:
+        sq._pool.shutdown()
+    assert np.array_equal(dst, src)
