@@ -423,10 +423,11 @@ def bench_cli(args) -> None:
         if r.returncode != 0:
             raise SystemExit(f"CLI failed ({r.returncode}): {r.stderr[-2000:]}")
         m = re.search(r"done in ([0-9.]+)s", r.stdout)
+        phases = dict((k, float(v)) for k, v in re.findall(r"(\w+) ([0-9.]+)", r.stdout.split("pipeline seconds", 1)[-1].split("\n", 1)[0].split(":", 1)[-1]))
         if i >= args.warmup:
-            runs.append((float(m.group(1)), wall))
-    q_s = statistics.median(x for x, _ in runs)
-    wall_s = statistics.median(y for _, y in runs)
+            runs.append((float(m.group(1)), wall, phases))
+    q_s = statistics.median(x for x, _, _ in runs)
+    wall_s = statistics.median(y for _, y, _ in runs)
     line = {"metric": f"CLI input GB/s (synthetic {args.model.upper()}-class bf16 GGUF -> {scheme}, imatrix)",
             "value": round(2 * n_w / q_s / 1e9, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(q_s * 1e3, 1), "higher_is_better": True, "scaling": "strong",
@@ -434,7 +435,8 @@ def bench_cli(args) -> None:
             "config": {"workload": f"BASELINE configs[{3 if args.model == '4b' else 4}]: {args.model} model, {scheme} + imatrix, "
                                    f"--gpus {args.gpus}, --mem {args.mem}", "weight_values": n_w,
                        "model_bytes": model.stat().st_size, "output_bytes": out.stat().st_size},
-            "quantize_s": round(q_s, 3), "cli_wall_s": round(wall_s, 2), "generate_s": gen_s}
+            "quantize_s": round(q_s, 3), "cli_wall_s": round(wall_s, 2), "generate_s": gen_s,
+            "pipeline_phase_s": runs[-1][2]}
     print(json.dumps(line), flush=True)
 
 

@@ -65,7 +65,7 @@ int ensure_device(int device, DeviceState** out) {
         cudaError_t e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
         if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
         e = qs::iq_tables_create(&d.iq);
-        if (e != cudaSuccess) return cuda_fail(e, "uploading lattice tables");
+        if (e != cudaSuccess) return cuda_fail(e, "uploading the lattice codebooks");
         cudaMemPoolProps props;
         memset(&props, 0, sizeof(props));
         props.allocType = cudaMemAllocationTypePinned;
@@ -217,6 +217,8 @@ QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_r
     a.nblk_row = k / ti->qk;
     a.nblk = n_rows * a.nblk_row;
     qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
+    if (is_iq(ggml_type) && (e = qs::iq_tables_ensure(d->iq, ggml_type)) != cudaSuccess)
+        return cuda_fail(e, "building lattice tables");
     e = is_iq(ggml_type) ? qs::launch_iq(ggml_type, a, ctx, d->iq) : qs::launch_kquant(ggml_type, a, ctx);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return QS_OK;

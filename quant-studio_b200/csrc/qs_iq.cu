@@ -19,6 +19,7 @@
 // memory, column (warp * 32 + lane): a term's address is the candidate's level bits,
 // shifted into bits 8..11, OR-ed with the lane's byte column, plus a constant row.
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "iq_grids.h"
@@ -41,7 +42,10 @@ struct IqGridDev {
 
 struct IqTables {
     IqGridDev g[5];
-    void* mem = nullptr;
+    void* mem = nullptr;              // the five codebooks
+    void* gmem[5] = {};               // each grid's neighbour tables, built on first use
+    bool built[5] = {};
+    std::mutex mu;
 };
 
 enum { G_IQ2XXS = 0, G_IQ2XS, G_IQ2S, G_IQ3XXS, G_IQ3S };
@@ -58,7 +62,8 @@ static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwa
     kmap16.assign(kmap.begin(), kmap.end());
     const int nidx = bits == 2 ? 6561 : 4096;
     nbr.assign(nidx, 0);
-    std::vector<int64_t> keys(G);
+    std::vector<int64_t> keys;
+    std::vector<int> dist(G);
     for (int idx = 0; idx < nidx; idx++) {
         int code = 0;
         if (bits == 2) {
@@ -71,6 +76,10 @@ static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwa
             nbr[idx] = 0x80000000u | (uint32_t)code;
             continue;
         }
+        // squared distances to every grid point; the list is every point within the nwant
+        // smallest distinct distances, in (distance, index) order: find the thresholds in
+        // one pass, then sort only the selected points
+        int thr[3] = {INT32_MAX, INT32_MAX, INT32_MAX};  // nwant <= 3 smallest distinct distances
         for (int i = 0; i < G; i++) {
             int d2 = 0;
             for (int j = 0; j < npos; j++) {
@@ -78,37 +87,50 @@ static void build_grid(const uint16_t* kgrid, int G, int bits, int npos, int nwa
                 int q = 2 * ((kgrid[i] >> (bits * j)) & mask) + 1;
                 d2 += (p - q) * (p - q);
             }
-            keys[i] = (int64_t)d2 * 65536 + i;
+            dist[i] = d2;
+            for (int w = 0; w < nwant; w++) {
+                if (d2 == thr[w]) break;
+                if (d2 < thr[w]) {
+                    for (int v = nwant - 1; v > w; v--) thr[v] = thr[v - 1];
+                    thr[w] = d2;
+                    break;
+                }
+            }
         }
+        int lim = thr[0];  // the largest threshold found (fewer than nwant distinct distances: all)
+        for (int w = 1; w < nwant; w++)
+            if (thr[w] != INT32_MAX) lim = thr[w];
+        keys.clear();
+        for (int i = 0; i < G; i++)
+            if (dist[i] <= lim) keys.push_back((int64_t)dist[i] * 65536 + i);
         std::sort(keys.begin(), keys.end());
-        int ndist = 0, n = 0;
-        int64_t prev = -1;
-        for (int i = 0; i < G; i++) {
-            int64_t d2 = keys[i] / 65536;
-            if (d2 != prev) { ndist++; prev = d2; }
-            if (ndist > nwant) break;
-            n++;
-        }
+        const int n = (int)keys.size();
         const int nq = (n + 3) / 4;  // quads of 4 codes, one 8-byte load each
         nbr[idx] = ((uint32_t)(list.size() / 4) << 9) | (uint32_t)nq;
         for (int i = 0; i < 4 * nq; i++) list.push_back(kgrid[keys[i < n ? i : n - 1] % 65536]);
     }
 }
 
-cudaError_t iq_tables_create(IqTables** out) {
-    struct Spec { const uint16_t* grid; int G, bits, npos, nwant; } specs[5] = {
-        {KGRID_2BIT_256, 256, 2, 8, 2}, {KGRID_2BIT_512, 512, 2, 8, 2}, {KGRID_2BIT_1024, 1024, 2, 8, 1},
-        {KGRID_3BIT_256, 256, 3, 4, 2}, {KGRID_3BIT_512, 512, 3, 4, 3}};
-    std::vector<uint32_t> nbr[5];
-    std::vector<uint16_t> list[5];
-    std::vector<int16_t> kmap[5];
-    size_t total = 0;
-    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
-    for (int t = 0; t < 5; t++) {
-        build_grid(specs[t].grid, specs[t].G, specs[t].bits, specs[t].npos, specs[t].nwant, nbr[t], list[t], kmap[t]);
-        if (list[t].size() / 4 > 65535) return cudaErrorInvalidValue;  // queue entries hold 16-bit quad offsets
-        total += al(specs[t].G * 2) + al(nbr[t].size() * 4) + al(list[t].size() * 2 + 16) + al(kmap[t].size() * 2);
+struct GridSpec { const uint16_t* grid; int G, bits, npos, nwant; };
+static const GridSpec kGrids[5] = {
+    {KGRID_2BIT_256, 256, 2, 8, 2}, {KGRID_2BIT_512, 512, 2, 8, 2}, {KGRID_2BIT_1024, 1024, 2, 8, 1},
+    {KGRID_3BIT_256, 256, 3, 4, 2}, {KGRID_3BIT_512, 512, 3, 4, 3}};
+
+static int grid_of(int type) {
+    switch (type) {
+    case QS_IQ2_XXS: return G_IQ2XXS;
+    case QS_IQ2_XS: return G_IQ2XS;
+    case QS_IQ2_S: return G_IQ2S;
+    case QS_IQ3_XXS: return G_IQ3XXS;
+    case QS_IQ3_S: return G_IQ3S;
+    default: return -1;
     }
+}
+
+// Uploads the five codebooks; the neighbour tables of a grid are built by iq_tables_ensure.
+cudaError_t iq_tables_create(IqTables** out) {
+    size_t total = 0;
+    for (const GridSpec& sp : kGrids) total += ((size_t)sp.G * 2 + 255) & ~(size_t)255;
     char* mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, total);
     if (e != cudaSuccess) return e;
@@ -117,24 +139,50 @@ cudaError_t iq_tables_create(IqTables** out) {
     size_t o = 0;
     for (int t = 0; t < 5; t++) {
         uint16_t* kg = reinterpret_cast<uint16_t*>(mem + o);
-        o += al(specs[t].G * 2);
-        uint32_t* nb = reinterpret_cast<uint32_t*>(mem + o);
-        o += al(nbr[t].size() * 4);
-        uint16_t* ls = reinterpret_cast<uint16_t*>(mem + o);
-        o += al(list[t].size() * 2 + 16);
-        int16_t* km = reinterpret_cast<int16_t*>(mem + o);
-        o += al(kmap[t].size() * 2);
-        if ((e = cudaMemcpy(kg, specs[t].grid, specs[t].G * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
-            (e = cudaMemcpy(nb, nbr[t].data(), nbr[t].size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
-            (e = cudaMemcpy(ls, list[t].data(), list[t].size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
-            (e = cudaMemcpy(km, kmap[t].data(), kmap[t].size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
+        o += ((size_t)kGrids[t].G * 2 + 255) & ~(size_t)255;
+        if ((e = cudaMemcpy(kg, kGrids[t].grid, kGrids[t].G * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
             cudaFree(mem);
             delete T;
             return e;
         }
-        T->g[t] = IqGridDev{kg, nb, ls, km, specs[t].G};
+        T->g[t] = IqGridDev{kg, nullptr, nullptr, nullptr, kGrids[t].G};
     }
     *out = T;
+    return cudaSuccess;
+}
+
+// Builds and uploads the neighbour tables of `type`'s grid once (thread-safe; the device
+// must be current).
+cudaError_t iq_tables_ensure(IqTables* T, int type) {
+    const int t = grid_of(type);
+    if (t < 0) return cudaSuccess;
+    std::lock_guard<std::mutex> lk(T->mu);
+    if (T->built[t]) return cudaSuccess;
+    std::vector<uint32_t> nbr;
+    std::vector<uint16_t> list;
+    std::vector<int16_t> kmap;
+    const GridSpec& sp = kGrids[t];
+    build_grid(sp.grid, sp.G, sp.bits, sp.npos, sp.nwant, nbr, list, kmap);
+    if (list.size() / 4 > 65535) return cudaErrorInvalidValue;  // queue entries hold 16-bit quad offsets
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    const size_t total = al(nbr.size() * 4) + al(list.size() * 2 + 16) + al(kmap.size() * 2);
+    char* mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, total);
+    if (e != cudaSuccess) return e;
+    uint32_t* nb = reinterpret_cast<uint32_t*>(mem);
+    uint16_t* ls = reinterpret_cast<uint16_t*>(mem + al(nbr.size() * 4));
+    int16_t* km = reinterpret_cast<int16_t*>(mem + al(nbr.size() * 4) + al(list.size() * 2 + 16));
+    if ((e = cudaMemcpy(nb, nbr.data(), nbr.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(ls, list.data(), list.size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(km, kmap.data(), kmap.size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
+        cudaFree(mem);
+        return e;
+    }
+    T->gmem[t] = mem;
+    T->g[t].nbr = nb;
+    T->g[t].list = ls;
+    T->g[t].kmap = km;
+    T->built[t] = true;
     return cudaSuccess;
 }
 
@@ -151,6 +199,7 @@ const uint16_t* iq_kgrid(const IqTables* t, int type) {
 
 void iq_tables_destroy(IqTables* t) {
     if (t) {
+        for (void* m : t->gmem) cudaFree(m);
         cudaFree(t->mem);
         delete t;
     }

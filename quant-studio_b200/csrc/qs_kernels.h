@@ -34,7 +34,8 @@ struct IqTables;  // per-device lattice tables (qs_iq.cu)
 
 cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx);
 cudaError_t launch_iq(int type, const QuantArgs& a, const LaunchCtx& ctx, const IqTables* t);
-cudaError_t iq_tables_create(IqTables** out);  // uploads to the current device
+cudaError_t iq_tables_create(IqTables** out);  // uploads the codebooks to the current device
+cudaError_t iq_tables_ensure(IqTables* t, int type);  // neighbour tables of type's grid, once
 void iq_tables_destroy(IqTables* t);
 const uint16_t* iq_kgrid(const IqTables* t, int type);  // IQ codebook (grid index -> code), else null
 

@@ -13,9 +13,15 @@ every tensor an aligned offset), so any chunk can be written the moment it is re
     (no f32 upcast), copies the blocks back and writes them with os.pwrite;
   * two slots per GPU, each with its own stream, so the host copy and the file write of
     one chunk overlap the device work of the other;
-  * the copy of a chunk from the mapped model into pinned memory is split over a shared
-    pool of host threads (numpy releases the GIL for it): one thread moves only a few GB/s
-    and takes the mapping's page faults alone, which made it the bottleneck of the CLI;
+  * the rows of a chunk reach pinned memory by positioned reads of the model file (the CLI
+    passes its descriptor), split over a shared pool of host threads (reading through the
+    mapping costs a page fault per 4 KiB on first touch; one thread moves only a few GB/s);
+  * a chunk's blocks go to the file on a writer thread while the worker reads the next
+    chunk; the slot waits for that write only before its output staging is reused;
+  * chunks are also capped at CHUNK_BYTES of source rows, so the pinned staging stays small
+    (page-locking memory costs about 0.5 s per GB) and large tensors pipeline in pieces;
+  * each slot owns its device copy of the importance weights, uploaded on the slot's own
+    stream: a chunk's kernel can never see the weights of the chunk after it;
   * passthrough tensors are copied with pwrite from the source mmap.
 No collective and no peer traffic: the GPUs share nothing but the queue.
 """
@@ -46,6 +52,8 @@ class QuantJob:
     out_offset: int           # absolute file offset of the tensor's data
     row_bytes: int            # packed bytes per row
     bytes_per_elem: int       # working-set heuristic for the chunk size
+    src_fd: int = -1          # when >= 0: read the rows from this file at src_offset instead
+    src_offset: int = 0       #   of copying them out of `rows` (the mapping), see _read_rows
 
 
 @dataclass
@@ -62,7 +70,8 @@ class _Slot:
         self.h_in = self.h_out = None
         self.d_in = self.d_out = None
         self.pending = None       # (nbytes, file offset) of the chunk in flight
-        self.qw = None            # the weights the chunk in flight reads: kept alive until it is retired
+        self.h_qw = self.d_qw = None  # this slot's importance weights: pinned staging, device copy
+        self.wfut = None              # the write of the slot's last chunk (reads h_out)
 
     @staticmethod
     def _grow_pinned(buf, nbytes):
@@ -80,7 +89,8 @@ class _Slot:
 class ShardedQuantizer:
     """Quantize a list of jobs across `devices`, writing into the open file `fd`."""
 
-    COPY_SLICE = 8 << 20  # bytes per host-copy task
+    COPY_SLICE = 8 << 20     # bytes per host read / write task
+    CHUNK_BYTES = 128 << 20  # source bytes per chunk at most
 
     def __init__(self, devices: list[torch.device], fd: int, mem_bytes: int, copy_threads: int | None = None):
         self.devices = devices
@@ -90,6 +100,36 @@ class ShardedQuantizer:
         self.stats: dict[str, float] = {}
         self.copy_threads = copy_threads or min(32, os.cpu_count() or 1)
         self._pool: ThreadPoolExecutor | None = None
+        self._writer: ThreadPoolExecutor | None = None
+        # seconds per phase, summed over the GPU workers (read / alloc / enqueue / wait / write)
+        self.timing = dict.fromkeys(("read", "alloc", "enqueue", "wait", "write"), 0.0)
+        self._tlock = threading.Lock()
+        self._max_in = self._max_out = self._max_k = 0  # largest chunk / row, for sizing the staging once
+
+    def _tick(self, key: str, t0: float) -> float:
+        t = time.perf_counter()
+        with self._tlock:
+            self.timing[key] += t - t0
+        return t
+
+    def _read_rows(self, dst: np.ndarray, fd: int, offset: int) -> None:
+        """Fill the 1-D uint8 array dst from file fd at offset, in slices on the copy pool."""
+        mv = memoryview(dst)
+
+        def read(a: int, b: int) -> None:
+            while a < b:
+                n = os.preadv(fd, [mv[a:b]], offset + a)
+                if n <= 0:
+                    raise OSError(f"short read at offset {offset + a}")
+                a += n
+
+        n = dst.size
+        if self._pool is None or n <= self.COPY_SLICE:
+            read(0, n)
+            return
+        futs = [self._pool.submit(read, a, min(n, a + self.COPY_SLICE)) for a in range(0, n, self.COPY_SLICE)]
+        for f in futs:
+            f.result()
 
     def _copy_rows(self, dst: np.ndarray, src: np.ndarray) -> None:
         """dst[:] = src for (n, row_bytes) arrays, in row slices on the copy pool."""
@@ -106,14 +146,25 @@ class ShardedQuantizer:
     def _chunks(self, jobs: list[QuantJob]):
         for j in jobs:
             n = j.rows.shape[0]
-            step = max(1, self.mem_bytes // max(1, j.k * j.bytes_per_elem))
+            step = max(1, min(self.mem_bytes // max(1, j.k * j.bytes_per_elem),
+                              self.CHUNK_BYTES // max(1, j.rows.shape[1])))
             for r0 in range(0, n, step):
                 yield j, r0, min(n, r0 + step)
 
     # -- one GPU -----------------------------------------------------------
     def _open(self, device: torch.device):
         torch.cuda.set_device(device)
-        return {"device": device, "slots": [_Slot(device), _Slot(device)], "next": 0, "qw": {}}
+        slots = [_Slot(device), _Slot(device)]
+        t0 = time.perf_counter()
+        for sl in slots:  # sized once for the largest chunk of the run
+            sl.h_in = _Slot._grow_pinned(None, self._max_in)
+            sl.h_out = _Slot._grow_pinned(None, self._max_out)
+            sl.d_in = _Slot._grow_dev(None, self._max_in, device)
+            sl.d_out = _Slot._grow_dev(None, self._max_out, device)
+            sl.h_qw = torch.empty(max(self._max_k, 1), dtype=torch.float32, pin_memory=True)
+            sl.d_qw = torch.empty(max(self._max_k, 1), dtype=torch.float32, device=device)
+        self._tick("alloc", t0)
+        return {"device": device, "slots": slots, "next": 0}
 
     def _submit(self, ctx, job: QuantJob, r0: int, r1: int):
         """Stage rows r0:r1 of `job`, run the kernel, start the copy back (asynchronous)."""
@@ -124,24 +175,28 @@ class ShardedQuantizer:
         n = r1 - r0
         in_bytes = n * job.rows.shape[1]
         out_bytes = n * job.row_bytes
+        t0 = time.perf_counter()
         slot.h_in = _Slot._grow_pinned(slot.h_in, in_bytes)
         slot.h_out = _Slot._grow_pinned(slot.h_out, out_bytes)
         slot.d_in = _Slot._grow_dev(slot.d_in, in_bytes, device)
         slot.d_out = _Slot._grow_dev(slot.d_out, out_bytes, device)
-        self._copy_rows(slot.h_in[:in_bytes].numpy().reshape(n, -1), job.rows[r0:r1])
+        t0 = self._tick("alloc", t0)
+        if job.src_fd >= 0:
+            self._read_rows(slot.h_in[:in_bytes].numpy(), job.src_fd, job.src_offset + r0 * job.rows.shape[1])
+        else:
+            self._copy_rows(slot.h_in[:in_bytes].numpy().reshape(n, -1), job.rows[r0:r1])
+        t0 = self._tick("read", t0)
+        if slot.wfut is not None:  # h_out is about to be overwritten by this chunk's blocks
+            slot.wfut.result()
+            slot.wfut = None
+            t0 = self._tick("write", t0)
         qw = None
-        if job.qw is not None:
-            cache = ctx["qw"]
-            if id(job) not in cache:
-                cache.clear()
-                cache[id(job)] = torch.from_numpy(np.ascontiguousarray(job.qw[:job.k], dtype=np.float32)).to(device)
-            qw = cache[id(job)]
-        # the other slot's kernel may still read the previous job's weights; holding them here
-        # keeps the caching allocator from giving their memory to the next upload
-        slot.qw = qw
+        if job.qw is not None:  # the slot is retired, so its staging is free
+            np.copyto(slot.h_qw[:job.k].numpy(), np.asarray(job.qw[:job.k], dtype=np.float32))
+            qw = slot.d_qw[:job.k]
         with torch.cuda.stream(slot.stream):
             if qw is not None:
-                slot.stream.wait_stream(torch.cuda.current_stream(device))
+                qw.copy_(slot.h_qw[:job.k], non_blocking=True)
             slot.d_in[:in_bytes].copy_(slot.h_in[:in_bytes], non_blocking=True)
             x = slot.d_in[:in_bytes].view(job.src_dtype).view(n, job.k)
             out = slot.d_out[:out_bytes].view(n, job.row_bytes)
@@ -149,22 +204,33 @@ class ShardedQuantizer:
             slot.h_out[:out_bytes].copy_(slot.d_out[:out_bytes], non_blocking=True)
             slot.event.record(slot.stream)
         slot.pending = (out_bytes, job.out_offset + r0 * job.row_bytes)
+        self._tick("enqueue", t0)
 
     def _drain(self, ctx):
         for slot in ctx["slots"]:
             self._retire(slot)
+        for slot in ctx["slots"]:
+            if slot.wfut is not None:
+                slot.wfut.result()
+                slot.wfut = None
 
     def _retire(self, slot: _Slot):
         """Wait for the slot's chunk and write its blocks to the file."""
         if slot.pending is None:
             return
         nbytes, off = slot.pending
+        t0 = time.perf_counter()
         slot.event.synchronize()
-        slot.qw = None
-        self._write(slot.h_out[:nbytes].numpy(), off)
+        self._tick("wait", t0)
+        buf = slot.h_out[:nbytes].numpy()
+        slot.wfut = self._writer.submit(self._write, buf, off) if self._writer else None
+        if slot.wfut is None:
+            self._write(buf, off)
         slot.pending = None
 
     def _write(self, buf: np.ndarray, off: int):
+        """Write buf at file offset off (positioned writes to one file serialize in the
+        kernel, so one thread per write)."""
         mv = memoryview(buf.reshape(-1).view(np.uint8))
         done = 0
         while done < len(mv):
@@ -189,12 +255,16 @@ class ShardedQuantizer:
     def run(self, jobs: list[QuantJob], copies: list[CopyJob] = ()) -> float:
         t0 = time.time()
         work: queue.Queue = queue.Queue()
-        for c in self._chunks(jobs):
-            work.put(c)
+        for j, r0, r1 in self._chunks(jobs):
+            self._max_in = max(self._max_in, (r1 - r0) * j.rows.shape[1])
+            self._max_out = max(self._max_out, (r1 - r0) * j.row_bytes)
+            self._max_k = max(self._max_k, j.k)
+            work.put((j, r0, r1))
         for _ in self.devices:
             work.put(None)
         lock = threading.Lock()
         self._pool = ThreadPoolExecutor(max_workers=self.copy_threads) if self.copy_threads > 1 else None
+        self._writer = ThreadPoolExecutor(max_workers=2 * len(self.devices)) if self.devices else None
         try:
             threads = [threading.Thread(target=self._worker, args=(d, work, lock), daemon=True) for d in self.devices]
             for t in threads:
@@ -204,9 +274,10 @@ class ShardedQuantizer:
             for t in threads:
                 t.join()
         finally:
-            if self._pool is not None:
-                self._pool.shutdown(wait=True)
-                self._pool = None
+            for ex in (self._pool, self._writer):
+                if ex is not None:
+                    ex.shutdown(wait=True)
+            self._pool = self._writer = None
         if self.error is not None:
             raise self.error
         return time.time() - t0

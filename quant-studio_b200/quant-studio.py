@@ -17,6 +17,7 @@ from __future__ import annotations
 import argparse
 import os
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -29,7 +30,7 @@ import gguf
 from gguf import GGMLQuantizationType, GGUFReader, GGUFValueType, GGUFWriter
 from gguf.constants import GGML_QUANT_SIZES, GGML_QUANT_VERSION
 
-from kernels import QUANT_TYPES, TORCH_DTYPES, scheme
+from kernels import QUANT_TYPES, TORCH_DTYPES, _native, scheme
 from kernels.pipeline import CopyJob, QuantJob, ShardedQuantizer
 
 
@@ -110,6 +111,27 @@ def pick_devices(device: str, ngpus: int) -> list[torch.device]:
     return [torch.device("cuda", first + i) for i in range(n)]
 
 
+def start_device_warmup(args) -> tuple[threading.Thread, dict]:
+    """Pick the devices and bring up their CUDA contexts and libqsb200 state on a background
+    thread, while the main thread reads and plans the model."""
+    box: dict = {}
+
+    def run() -> None:
+        try:
+            devs = pick_devices(args.device, args.gpus)
+            for d in devs:
+                torch.cuda.set_device(d)
+                torch.empty(1, device=d)
+                _native.check(_native.lib().qs_init(d.index))
+            box["devices"] = devs
+        except BaseException as e:  # re-raised on the main thread
+            box["error"] = e
+
+    t = threading.Thread(target=run, daemon=True)
+    t.start()
+    return t, box
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description="B200 GGUF quantizer, drop-in for llama-quantize",
                                  formatter_class=argparse.RawDescriptionHelpFormatter,
@@ -139,6 +161,7 @@ def main() -> None:
     rej.add_argument("--keep-split", action="store_true", help=argparse.SUPPRESS)
     rej.add_argument("--override-kv", action="append", default=[], help=argparse.SUPPRESS)
     args = ap.parse_args()
+    warm = None if args.dry_run else start_device_warmup(args)
 
     for flag, val in (("--allow-requantize", args.allow_requantize), ("--include-weights", args.include_weights),
                       ("--exclude-weights", args.exclude_weights), ("--prune-layers", args.prune_layers),
@@ -239,7 +262,10 @@ def main() -> None:
         print(f"dry run: {fmt_size(tin)} -> {fmt_size(tout)} tensor data ({tout / max(tin, 1) * 100:.1f}%)")
         return
 
-    devices = pick_devices(args.device, args.gpus)
+    warm[0].join()
+    if "error" in warm[1]:
+        raise warm[1]["error"]
+    devices = warm[1]["devices"]
     print(f"qs-b200: {args.input} -> {out_path} [{opt.name}] gpus={len(devices)} mem={args.mem}")
     if args.imatrix is not None:
         print(f"imatrix: {len(imatrix)} entries from {args.imatrix}")
@@ -262,6 +288,7 @@ def main() -> None:
     align = writer.data_alignment
     pos = GGUFWriter.ggml_pad(fout.tell(), align)
 
+    src_fd = os.open(args.input, os.O_RDONLY)  # rows are read with pread, not through the mapping
     jobs, copies, offsets = [], [], []
     for t, dst, spec in plans:
         offsets.append(pos)
@@ -270,14 +297,18 @@ def main() -> None:
             qw = imatrix[t.name][:k] if (spec.uses_imatrix and t.name in imatrix) else None
             rows = t.data.reshape(-1, t.data.shape[-1]).view(np.uint8)
             jobs.append(QuantJob(t.name, rows, TORCH_DTYPES[t.tensor_type], k, int(dst), qw, pos,
-                                 out_row_bytes_for(k, dst), spec.bytes_per_elem))
+                                 out_row_bytes_for(k, dst), spec.bytes_per_elem, src_fd, int(t.data_offset)))
         else:
             copies.append(CopyJob(t.name, t.data, pos))
         pos += GGUFWriter.ggml_pad(out_nbytes(t, dst), align)
     fd = fout.fileno()
     os.ftruncate(fd, pos)  # zero padding between tensors, like the reference's pad_to_alignment
 
-    dt = ShardedQuantizer(devices, fd, mem_bytes).run(jobs, copies)
+    sq = ShardedQuantizer(devices, fd, mem_bytes)
+    try:
+        dt = sq.run(jobs, copies)
+    finally:
+        os.close(src_fd)
     tin = tout = 0
     for i, (t, dst, _) in enumerate(plans):
         nb = out_nbytes(t, dst)
@@ -289,6 +320,7 @@ def main() -> None:
     os.fsync(fd)
     writer.close()
     print(f"done in {dt:.3f}s: {fmt_size(tin)} -> {fmt_size(tout)} ({tout / max(tin, 1) * 100:.1f}%)")
+    print("pipeline seconds (summed over GPU workers): " + ", ".join(f"{k} {v:.3f}" for k, v in sq.timing.items()))
 
 
 if __name__ == "__main__":

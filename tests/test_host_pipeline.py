@@ -118,3 +118,26 @@ def test_host_copy_split_over_the_pool():
     finally:
         sq._pool.shutdown()
     assert np.array_equal(dst, src)
+
+
+def test_rows_read_from_the_file(tmp_path):
+    """The positioned-read path fills the staging buffer with exactly the file's bytes."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from kernels.pipeline import ShardedQuantizer
+
+    data = np.random.default_rng(1).integers(0, 256, size=30_000_123, dtype=np.uint8)
+    path = tmp_path / "src.bin"
+    data.tofile(path)
+    fd = os.open(path, os.O_RDONLY)
+    sq = ShardedQuantizer([], fd=-1, mem_bytes=1 << 30, copy_threads=4)
+    try:
+        for pool in (None, ThreadPoolExecutor(max_workers=4)):
+            sq._pool = pool
+            dst = np.zeros(20_000_000, dtype=np.uint8)
+            sq._read_rows(dst, fd, 5_000_007)
+            assert np.array_equal(dst, data[5_000_007:25_000_007])
+            if pool is not None:
+                pool.shutdown()
+    finally:
+        os.close(fd)
