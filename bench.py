@@ -18,6 +18,9 @@ only for the barrier and the max-over-ranks of the timings).
   roofline  the Q4_K kernel against the FP32 lane-op ceiling (148 SMs x 128 lanes x SM clock):
          algorithmic ops = 655 per value (37 x 17 per candidate step + 11 initial + 3 sums
          + 5 weights + 7 requant/pack); plus the HBM view of the same launches
+cpu_baseline  the CPU restatement of the reference's algorithm (oracle/) on all host cores over
+         a bounded sample of the workload; the same sample is quantized on the GPU and
+         `identical_blocks` is the fraction of blocks that match (the metric's identical-block %)
 --impl reference: the CPU restatement of the reference's algorithm (oracle/) on all host
 cores over a bounded sample of the same workload (the reference itself is Python/torch and
 cannot travel to the GPU host; oracle/ is its bit-exact C port).
@@ -164,7 +167,8 @@ def run_reference(args, config: dict) -> None:
         times.append(time.perf_counter() - t0)
     dt = statistics.median(times)
     gbs = x.size * 2 / dt / 1e9
-    line = {"impl": "reference", "metric": "input GB/s quantized (bf16->q4_k, imatrix)", "value": round(gbs, 6),
+    line = {"impl": "reference", "value": round(gbs, 6),
+            "metric": f"input GB/s quantized (bf16->{args.qtype}{', imatrix' if args.imatrix else ''})",
             "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "config": config,
@@ -318,7 +322,11 @@ def main() -> None:
                                    for i, (r, c) in enumerate(SHAPES_C2) if i in (0, len(SHAPES_C2) - 1)},
             "e2e": e2e}
     if rank == 0 and world == 1 and args.cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args)
+        def gpu_quantize(a, qw):
+            xd = torch.from_numpy(a).to(device).to(torch.bfloat16)  # a holds bf16-representable values
+            q = None if qw is None else torch.from_numpy(qw).to(device)
+            return _native.quantize(gt, xd, q).cpu().numpy()
+        line["cpu_baseline"] = cpu_baseline(args, gpu_quantize)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -504,8 +512,10 @@ def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, wor
             "matches_device_resident_output": ok}
 
 
-def cpu_baseline(args) -> dict:
-    """The oracle (C port of the reference algorithm) on this host's cores, bounded sample."""
+def cpu_baseline(args, gpu_quantize=None) -> dict:
+    """The oracle (C port of the reference algorithm) on this host's cores, bounded sample; with
+    gpu_quantize, the same sample is also quantized on the GPU and the fraction of identical
+    blocks reported (the identical-block part of the metric)."""
     import oracle
 
     cores = os.cpu_count() or 1
@@ -523,11 +533,18 @@ def cpu_baseline(args) -> dict:
     a[m] = rng.normal(0.0, 0.5, int(m.sum()))
     a = ((a.astype(np.float32).view(np.uint32) + 0x8000) & 0xFFFF0000).view(np.float32)
     t0 = time.perf_counter()
-    oracle.quantize(args.qtype, a, qw, nthreads=cores)
+    ref = oracle.quantize(args.qtype, a, qw, nthreads=cores)
     dt = time.perf_counter() - t0
-    return {"value": round(a.size * 2 / dt / 1e9, 6), "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{rows} rows x {k} values ({a.size * 2 / 1e6:.1f} MB bf16) of the benchmark distribution, "
-                      f"{dt:.1f} s on {cores} threads"}
+    out = {"value": round(a.size * 2 / dt / 1e9, 6), "unit": "GB/s", "cores": cores, "kind": "port",
+           "sample": f"{rows} rows x {k} values ({a.size * 2 / 1e6:.1f} MB bf16) of the benchmark distribution, "
+                     f"{dt:.1f} s on {cores} threads"}
+    if gpu_quantize is not None:
+        got = gpu_quantize(a, qw)
+        bb = ref.shape[1] // (k // (32 if args.qtype == "q4_0" else 256))
+        same = (got.reshape(-1, bb) == ref.reshape(-1, bb)).all(1)
+        out["identical_blocks"] = round(float(same.mean()), 6)
+        out["blocks_compared"] = int(same.size)
+    return out
 
 
 if __name__ == "__main__":
