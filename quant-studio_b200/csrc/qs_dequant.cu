@@ -277,31 +277,51 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
     const bool packed = a.src_row_bytes == a.nblk_row * D::BB;
     double acc_w = 0.0, acc = 0.0;
 
+    // Packed rows: a tile is one contiguous span of nb * BB bytes, at most one 16-byte body
+    // chunk plus a head and a tail byte per thread. The next tile's share is loaded into
+    // registers before the current tile is decoded, so the load latency overlaps the decode
+    // and the stores; the share lands in shared memory at s_blk + (address & 15), so the
+    // 16-byte aligned body moves with 16-byte stores.
+    static_assert((BPT * D::BB) / 16 + 1 <= DQ_THREADS, "one body chunk per thread");
+    struct Share {
+        uint4 v;
+        uint8_t h, tl;
+        int mis, head, body, nbytes;
+    };
+    auto fetch = [&](int64_t tile, Share& sh) {
+        const int64_t b0 = tile * BPT;
+        const uint8_t* g = a.src + b0 * D::BB;
+        sh.nbytes = (int)min((int64_t)BPT, a.nblk - b0) * D::BB;
+        sh.mis = (int)((uintptr_t)g & 15);
+        sh.head = min((16 - sh.mis) & 15, sh.nbytes);
+        sh.body = (sh.nbytes - sh.head) / 16;
+        if (tid < sh.body) sh.v = __ldg(reinterpret_cast<const uint4*>(g + sh.head) + tid);
+        if (tid < sh.head) sh.h = __ldg(g + tid);
+        const int ti = sh.head + 16 * sh.body + tid;
+        if (ti < sh.nbytes) sh.tl = __ldg(g + ti);
+    };
+    Share cur;
+    if (packed && (int64_t)blockIdx.x * BPT < a.nblk) fetch(blockIdx.x, cur);
+
     for (int64_t tile = blockIdx.x; tile * BPT < a.nblk; tile += gridDim.x) {
         const int64_t b0 = tile * BPT;
         const int nb = (int)min((int64_t)BPT, a.nblk - b0);
         const bool live = lb < nb;
         const int64_t b = b0 + lb;
         // the source values and weights do not depend on the blocks: in flight with the staging
-        float xv[8], w[8];
+        float cx[8], cw[8];
         if (MODE != DQ_DECODE && live) {
             const int64_t row = b / a.nblk_row, col = (b - row * a.nblk_row) * D::QK + 8 * t;
-            load_x8(a.x, row * a.k + col, a.x_type, xv);
-            if (a.qw) load_f32<8>(a.qw + col, w);
+            load_x8(a.x, row * a.k + col, a.x_type, cx);
+            if (a.qw) load_f32<8>(a.qw + col, cw);
         }
         const uint8_t* tb;
         if (packed) {
-            // one contiguous span of nb * BB bytes, placed at s_blk + (address & 15) so the
-            // 16-byte aligned body moves with 16-byte loads and stores
-            const uint8_t* g = a.src + b0 * D::BB;
-            const int mis = (int)((uintptr_t)g & 15), nbytes = nb * D::BB;
-            const int head = min((16 - mis) & 15, nbytes), body = (nbytes - head) / 16;
-            uint8_t* sp = s_blk + mis;
-            for (int i = tid; i < head; i += DQ_THREADS) sp[i] = __ldg(g + i);
-            const uint4* g4 = reinterpret_cast<const uint4*>(g + head);
-            uint4* s4 = reinterpret_cast<uint4*>(sp + head);
-            for (int i = tid; i < body; i += DQ_THREADS) s4[i] = __ldg(g4 + i);
-            for (int i = head + 16 * body + tid; i < nbytes; i += DQ_THREADS) sp[i] = __ldg(g + i);
+            uint8_t* sp = s_blk + cur.mis;
+            if (tid < cur.body) reinterpret_cast<uint4*>(sp + cur.head)[tid] = cur.v;
+            if (tid < cur.head) sp[tid] = cur.h;
+            const int ti = cur.head + 16 * cur.body + tid;
+            if (ti < cur.nbytes) sp[ti] = cur.tl;
             tb = sp;
         } else {
             for (int i = tid; i < nb * D::BB; i += DQ_THREADS) {
@@ -311,6 +331,8 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
             }
             tb = s_blk;
         }
+        __syncthreads();
+        if (packed && (tile + gridDim.x) * BPT < a.nblk) fetch(tile + gridDim.x, cur);  // the next tile
         __syncthreads();
         if (live) {
             float v[8];
@@ -326,9 +348,9 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
                 float fw = 0.0f, f2 = 0.0f;
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const float e = v[i] - xv[i];
+                    const float e = v[i] - cx[i];
                     const float ee = e * e;
-                    const float we = a.qw ? w[i] * ee : ee;
+                    const float we = a.qw ? cw[i] * ee : ee;
                     f2 = i == 0 ? ee : f2 + ee;
                     fw = i == 0 ? we : fw + we;
                 }

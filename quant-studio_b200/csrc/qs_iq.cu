@@ -211,34 +211,37 @@ void iq_tables_destroy(IqTables* t) {
 enum SumKind { SUM_TORCH, SUM_TREE };
 enum Reproj { RP_ALL_PROJ, RP_OFFGRID_NEED, RP_OFFGRID_REDO, RP_ALL_REDO };
 
+// ONE_SEARCH_SITE: the final reprojection runs as the last pass of the sweep loop, so the
+// search code is inlined once instead of twice (smaller code; measured faster for the IQ2
+// grids, slower for IQ3, where the two sites stay).
 template <int T> struct IqT;
 template <> struct IqT<QS_IQ2_XXS> {
     static constexpr int GS = 32, NSUB = 4, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 13, BB = 66, GID = G_IQ2XXS;
-    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = true;
+    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = true, ONE_SEARCH_SITE = true;
     static constexpr int SUMK = SUM_TORCH, RP = RP_ALL_PROJ;
     static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
 };
 template <> struct IqT<QS_IQ2_XS> {
     static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 74, GID = G_IQ2XS;
-    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
+    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false, ONE_SEARCH_SITE = true;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
     static constexpr float EPS = EPS15, SIGFAC = 1.0f, DMUL = 1.0f;
 };
 template <> struct IqT<QS_IQ2_S> {
     static constexpr int GS = 16, NSUB = 2, NPOS = 8, BITS = 2, NLEV = 4, MAXL = 2, NSTEP = 19, BB = 82, GID = G_IQ2S;
-    static constexpr bool PARITY = false, ACT_GT0 = false, INIT_QP = false;
+    static constexpr bool PARITY = false, ACT_GT0 = false, INIT_QP = false, ONE_SEARCH_SITE = true;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_NEED;
     static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 0.9875f;
 };
 template <> struct IqT<QS_IQ3_XXS> {
     static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 31, BB = 98, GID = G_IQ3XXS;
-    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false;
+    static constexpr bool PARITY = true, ACT_GT0 = false, INIT_QP = false, ONE_SEARCH_SITE = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_OFFGRID_REDO;
     static constexpr float EPS = EPS8, SIGFAC = 2.0f, DMUL = 1.0125f;
 };
 template <> struct IqT<QS_IQ3_S> {
     static constexpr int GS = 32, NSUB = 8, NPOS = 4, BITS = 3, NLEV = 8, MAXL = 7, NSTEP = 19, BB = 110, GID = G_IQ3S;
-    static constexpr bool PARITY = false, ACT_GT0 = true, INIT_QP = false;
+    static constexpr bool PARITY = false, ACT_GT0 = true, INIT_QP = false, ONE_SEARCH_SITE = false;
     static constexpr int SUMK = SUM_TREE, RP = RP_ALL_REDO;
     static constexpr float EPS = 0.0f, SIGFAC = 2.0f, DMUL = 1.033f;
 };
@@ -633,83 +636,164 @@ __global__ void __launch_bounds__(IQ_WARPS * 32, IQ_MIN_CTAS) iq_kernel(QuantArg
         for (int s = 0; s < NSUB; s++) cur[s] = cur0;  // grid index 0; og_init: IQ3_S starts off-grid
         __syncwarp();
 
-        // sweep over the candidate scales, NB steps per batch of searches
-        for (int s0 = 0; s0 < Tr::NSTEP; s0 += NB) {
-            const int nb = min(NB, Tr::NSTEP - s0);
-            // all codes of the batch first, so their table loads are in flight together
-            uint32_t nv[NB][NSUB];
-#pragma unroll
-            for (int j = 0; j < NB; j++) {
-                if (j < nb) {
-                    const float inv = r * s_c[s0 + j];
-                    W.psc[lane][j] = rcp_rn(inv);
-#pragma unroll
-                    for (int q = 0; q < NSUB; q++) nv[j][q] = __ldg(G.nbr + iq_index<Tr>(xval, q, inv));
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < NB; j++) {
-                if (j < nb) {
-                    uint32_t mask = 0;
-#pragma unroll
+        bool redo = false;
+        if (Tr::ONE_SEARCH_SITE) {
+            // sweep over the candidate scales, NB steps per batch of searches; the pass after the
+            // last batch is the final reprojection at the accepted scale (one search call site)
+            for (int s0 = 0;; s0 += NB) {
+                const bool final_pass = s0 >= Tr::NSTEP;
+                const int nb = final_pass ? 0 : min(NB, Tr::NSTEP - s0);
+                if (!final_pass) {
+                    // all codes of the batch first, so their table loads are in flight together
+                    uint32_t nv[NB][NSUB];
+    #pragma unroll
+                    for (int j = 0; j < NB; j++) {
+                        if (j < nb) {
+                            const float inv = r * s_c[s0 + j];
+                            W.psc[lane][j] = rcp_rn(inv);
+    #pragma unroll
+                            for (int q = 0; q < NSUB; q++) nv[j][q] = __ldg(G.nbr + iq_index<Tr>(xval, q, inv));
+                        }
+                    }
+    #pragma unroll
+                    for (int j = 0; j < NB; j++) {
+                        if (j < nb) {
+                            uint32_t mask = 0;
+    #pragma unroll
+                            for (int q = 0; q < NSUB; q++) {
+                                const uint32_t v = nv[j][q];
+                                if (v >> 31) W.win[lane][j * NSUB + q] = v & 0xFFFF;
+                                else mask |= 1u << q;
+                            }
+                            iq_enqueue<Tr>(W, lane, mask, nv[j], j);
+                        }
+                    }
+                } else {
+                    // final reprojection at the accepted scale + least-squares refit
+                    bool anyoff = false, allon = true;
+    #pragma unroll
+                    for (int q = 0; q < NSUB; q++) { anyoff |= (cur[q] & IQ_SEARCHED) != 0; allon &= (cur[q] & IQ_SEARCHED) == 0; }
+                    float inv;
+                    if (Tr::RP == RP_ALL_PROJ) {
+                        redo = active && scale > 0.0f;
+                        inv = rcp_rn(redo ? scale : 1.0f);
+                    } else if (Tr::RP == RP_OFFGRID_NEED) {
+                        redo = active && scale > 0.0f && !allon;
+                        inv = rcp_rn(scale > 0.0f ? scale : 1.0f);
+                    } else {
+                        redo = active && anyoff && scale > 0.0f;
+                        inv = rcp_rn(redo ? scale : 1.0f);
+                    }
+                    W.psc[lane][NB] = scale;
+                    uint32_t v[NSUB], mask = 0;
+    #pragma unroll
                     for (int q = 0; q < NSUB; q++) {
-                        const uint32_t v = nv[j][q];
-                        if (v >> 31) W.win[lane][j * NSUB + q] = v & 0xFFFF;
+                        const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & IQ_SEARCHED));
+                        // not reprojected: keep the current code (read back below without its flag)
+                        v[q] = want ? __ldg(G.nbr + iq_index<Tr>(xval, q, inv)) : 0x80000000u | cur[q];
+                    }
+    #pragma unroll
+                    for (int q = 0; q < NSUB; q++) {
+                        if (v[q] >> 31) W.win[lane][q] = v[q] & 0xFFFF;
                         else mask |= 1u << q;
                     }
-                    iq_enqueue<Tr>(W, lane, mask, nv[j], j);
+                    __syncwarp();
+                    iq_enqueue<Tr>(W, lane, mask, v, IQ_FINAL);
                 }
+                iq_flush<Tr>(W, G, lane);
+                if (final_pass) break;
+                for (int j = 0; j < nb; j++) {
+                    float qv[GS], sumqx, sumq2;
+                    iq_decode<Tr>(&W.win[lane][j * NSUB], qv);
+                    iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
+                    if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
+                        const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
+                        scale = ns;
+                        best = ns * sumqx;
+    #pragma unroll
+                        for (int q = 0; q < NSUB; q++) cur[q] = W.win[lane][j * NSUB + q];
+                    }
+                }
+                __syncwarp();
+            }
+        } else {
+            // sweep over the candidate scales, NB steps per batch of searches
+            for (int s0 = 0; s0 < Tr::NSTEP; s0 += NB) {
+                const int nb = min(NB, Tr::NSTEP - s0);
+                // all codes of the batch first, so their table loads are in flight together
+                uint32_t nv[NB][NSUB];
+    #pragma unroll
+                for (int j = 0; j < NB; j++) {
+                    if (j < nb) {
+                        const float inv = r * s_c[s0 + j];
+                        W.psc[lane][j] = rcp_rn(inv);
+    #pragma unroll
+                        for (int q = 0; q < NSUB; q++) nv[j][q] = __ldg(G.nbr + iq_index<Tr>(xval, q, inv));
+                    }
+                }
+    #pragma unroll
+                for (int j = 0; j < NB; j++) {
+                    if (j < nb) {
+                        uint32_t mask = 0;
+    #pragma unroll
+                        for (int q = 0; q < NSUB; q++) {
+                            const uint32_t v = nv[j][q];
+                            if (v >> 31) W.win[lane][j * NSUB + q] = v & 0xFFFF;
+                            else mask |= 1u << q;
+                        }
+                        iq_enqueue<Tr>(W, lane, mask, nv[j], j);
+                    }
+                }
+                iq_flush<Tr>(W, G, lane);
+                for (int j = 0; j < nb; j++) {
+                    float qv[GS], sumqx, sumq2;
+                    iq_decode<Tr>(&W.win[lane][j * NSUB], qv);
+                    iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
+                    if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
+                        const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
+                        scale = ns;
+                        best = ns * sumqx;
+    #pragma unroll
+                        for (int q = 0; q < NSUB; q++) cur[q] = W.win[lane][j * NSUB + q];
+                    }
+                }
+                __syncwarp();
+            }
+
+            // final reprojection at the accepted scale + least-squares refit
+            bool anyoff = false, allon = true;
+    #pragma unroll
+            for (int q = 0; q < NSUB; q++) { anyoff |= (cur[q] & IQ_SEARCHED) != 0; allon &= (cur[q] & IQ_SEARCHED) == 0; }
+            float inv;
+            if (Tr::RP == RP_ALL_PROJ) {
+                redo = active && scale > 0.0f;
+                inv = rcp_rn(redo ? scale : 1.0f);
+            } else if (Tr::RP == RP_OFFGRID_NEED) {
+                redo = active && scale > 0.0f && !allon;
+                inv = rcp_rn(scale > 0.0f ? scale : 1.0f);
+            } else {
+                redo = active && anyoff && scale > 0.0f;
+                inv = rcp_rn(redo ? scale : 1.0f);
+            }
+            W.psc[lane][NB] = scale;
+            {
+                uint32_t v[NSUB], mask = 0;
+    #pragma unroll
+                for (int q = 0; q < NSUB; q++) {
+                    const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & IQ_SEARCHED));
+                    // not reprojected: keep the current code (read back below without its flag)
+                    v[q] = want ? __ldg(G.nbr + iq_index<Tr>(xval, q, inv)) : 0x80000000u | cur[q];
+                }
+    #pragma unroll
+                for (int q = 0; q < NSUB; q++) {
+                    if (v[q] >> 31) W.win[lane][q] = v[q] & 0xFFFF;
+                    else mask |= 1u << q;
+                }
+                __syncwarp();
+                iq_enqueue<Tr>(W, lane, mask, v, IQ_FINAL);
             }
             iq_flush<Tr>(W, G, lane);
-            for (int j = 0; j < nb; j++) {
-                float qv[GS], sumqx, sumq2;
-                iq_decode<Tr>(&W.win[lane][j * NSUB], qv);
-                iq_sums<Tr>(w, xval, qv, sumqx, sumq2);
-                if (active && sumq2 > 0.0f && sumqx * sumqx > best * sumq2) {
-                    const float ns = __fdiv_rn(sumqx, sumq2 < F32_TINY ? F32_TINY : sumq2);
-                    scale = ns;
-                    best = ns * sumqx;
-#pragma unroll
-                    for (int q = 0; q < NSUB; q++) cur[q] = W.win[lane][j * NSUB + q];
-                }
-            }
-            __syncwarp();
         }
-
-        // final reprojection at the accepted scale + least-squares refit
-        bool anyoff = false, allon = true;
-#pragma unroll
-        for (int q = 0; q < NSUB; q++) { anyoff |= (cur[q] & IQ_SEARCHED) != 0; allon &= (cur[q] & IQ_SEARCHED) == 0; }
-        bool redo;
-        float inv;
-        if (Tr::RP == RP_ALL_PROJ) {
-            redo = active && scale > 0.0f;
-            inv = rcp_rn(redo ? scale : 1.0f);
-        } else if (Tr::RP == RP_OFFGRID_NEED) {
-            redo = active && scale > 0.0f && !allon;
-            inv = rcp_rn(scale > 0.0f ? scale : 1.0f);
-        } else {
-            redo = active && anyoff && scale > 0.0f;
-            inv = rcp_rn(redo ? scale : 1.0f);
-        }
-        W.psc[lane][NB] = scale;
-        {
-            uint32_t v[NSUB], mask = 0;
-#pragma unroll
-            for (int q = 0; q < NSUB; q++) {
-                const bool want = redo && (Tr::RP == RP_ALL_PROJ || Tr::RP == RP_ALL_REDO || (cur[q] & IQ_SEARCHED));
-                // not reprojected: keep the current code (read back below without its flag)
-                v[q] = want ? __ldg(G.nbr + iq_index<Tr>(xval, q, inv)) : 0x80000000u | cur[q];
-            }
-#pragma unroll
-            for (int q = 0; q < NSUB; q++) {
-                if (v[q] >> 31) W.win[lane][q] = v[q] & 0xFFFF;
-                else mask |= 1u << q;
-            }
-            __syncwarp();
-            iq_enqueue<Tr>(W, lane, mask, v, IQ_FINAL);
-        }
-        iq_flush<Tr>(W, G, lane);
         uint32_t fin[NSUB];
 #pragma unroll
         for (int q = 0; q < NSUB; q++) fin[q] = W.win[lane][q] & 0xFFFF;
