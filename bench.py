@@ -48,7 +48,17 @@ SHAPES_C2 = [(4096, 4096)] * 4 + [(14336, 4096)] * 4
 NAMES_C2 = [f"blk.{i}.attn_q.weight" for i in range(4)] + [f"blk.{i}.ffn_up.weight" for i in range(4)]
 # algorithmic FP32 lane ops per value for each (type, imatrix) the bench can time
 ALG_OPS = {("q4_k", True): 655, ("q4_k", False): 21 * 17 + 11 + 3 + 4 + 7,
-           ("q6_k", False): 19 * 9 + 20, ("q6_k", True): 19 * 9 + 18, ("q4_0", False): 10}
+           # Q5_K / Q2_K with imatrix: the same make_qkx search (37 steps x 17 lane ops per value)
+           ("q5_k", True): 655, ("q2_k", True): 655,
+           ("q6_k", False): 19 * 9 + 20, ("q6_k", True): 19 * 9 + 18, ("q4_0", False): 10,
+           # IQ lattice searches, counted on the benchmark distribution (off-grid problems and
+           # neighbour-list lengths from an instrumented run): candidates per value x (4 ops per
+           # position + 1 compare) + sweep steps x 12 (levels, accept sums) + 15 (weights,
+           # signs) [+ 110 for IQ2_XXS's initial make_qp fit]; candidates per value 39.1 /
+           # 93.3 / 13.3 / 50.8 / 38.9
+           ("iq2_xxs", True): round(39.1 * 33) + 14 * 12 + 15 + 110, ("iq2_xs", True): round(93.3 * 33) + 20 * 12 + 15,
+           ("iq2_s", True): round(13.3 * 33) + 20 * 12 + 15, ("iq3_xxs", True): round(50.8 * 17) + 32 * 12 + 15,
+           ("iq3_s", True): round(38.9 * 17) + 20 * 12 + 15}
 ALG_BYTES_OUT = {"q4_0": 18 / 32, "q2_k": 84 / 256, "q3_k": 110 / 256, "q4_k": 144 / 256,
                  "q5_k": 176 / 256, "q6_k": 210 / 256, "iq4_xs": 136 / 256, "iq2_xxs": 66 / 256,
                  "iq2_xs": 74 / 256, "iq2_s": 82 / 256, "iq3_xxs": 98 / 256, "iq3_s": 110 / 256}
@@ -292,8 +302,10 @@ def main() -> None:
     hbm = {"bound": "hbm", "achieved": round(alg_bytes / (launch_ms * 1e-3) / 1e9, 2), "peak": peaks["hbm_gbs"],
            "unit": "GB/s", "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"}
     hbm["frac"] = round(hbm["achieved"] / hbm["peak"], 4)
-    if ops is not None:
-        lane_peak = sm_count * 128 * sm_mhz * 1e6 / 1e12
+    # the binding roofline is the slower of the two bounds: bytes at HBM bandwidth and
+    # algorithmic lane ops at the FP32 lane peak; the other one is reported inside it
+    lane_peak = sm_count * 128 * sm_mhz * 1e6 / 1e12
+    if ops is not None and ops / (lane_peak * 1e12) > (2 + ALG_BYTES_OUT[args.qtype]) / (peaks["hbm_gbs"] * 1e9):
         roof = {"bound": "fp32-lane", "achieved": round(ops * elems_per_launch / (launch_ms * 1e-3) / 1e12, 3),
                 "peak": round(lane_peak, 3), "unit": "Tops/s",
                 "peak_source": f"{sm_count} SMs x 128 FP32 lanes x {sm_mhz:.0f} MHz median SM clock in the timed region",
@@ -301,6 +313,10 @@ def main() -> None:
         roof["frac"] = round(roof["achieved"] / roof["peak"], 4)
     else:
         roof = dict(hbm, traffic=None)
+        if ops is not None:
+            lane_ach = ops * elems_per_launch / (launch_ms * 1e-3) / 1e12
+            roof["fp32_lane"] = {"achieved": round(lane_ach, 3), "peak": round(lane_peak, 3), "unit": "Tops/s",
+                                 "ops_per_value": ops, "frac": round(lane_ach / lane_peak, 4)}
     prof = ROOT / "profiles" / f"traffic_{args.qtype}{'_imat' if args.imatrix else ''}.json"
     if prof.exists():
         roof["traffic"] = json.loads(prof.read_text()).get("bytes_per_value_launch")
