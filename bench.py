@@ -13,8 +13,8 @@ only for the barrier and the max-over-ranks of the timings).
 
   value  input GB/s with inputs resident in HBM (whole job, all ranks)
   e2e    the same metric through the public API from pinned host buffers: per step every
-         tensor is copied host->device, quantized and its blocks copied back to host, with
-         copies and kernels overlapped on two streams
+         tensor is copied host->device, quantized and its blocks copied back to host, in
+         row chunks with the copies and kernels overlapped on three streams
   roofline  the Q4_K kernel against the FP32 lane-op ceiling (148 SMs x 128 lanes x SM clock):
          algorithmic ops = 655 per value (37 x 17 per candidate step + 11 initial + 3 sums
          + 5 weights + 7 requant/pack); plus the HBM view of the same launches
@@ -50,7 +50,7 @@ NAMES_C2 = [f"blk.{i}.attn_q.weight" for i in range(4)] + [f"blk.{i}.ffn_up.weig
 ALG_OPS = {("q4_k", True): 655, ("q4_k", False): 21 * 17 + 11 + 3 + 4 + 7,
            # Q5_K / Q2_K with imatrix: the same make_qkx search (37 steps x 17 lane ops per value)
            ("q5_k", True): 655, ("q2_k", True): 655,
-           ("q6_k", False): 19 * 9 + 20, ("q6_k", True): 19 * 9 + 18, ("q4_0", False): 10,
+           ("q6_k", False): 19 * 9 + 20, ("q6_k", True): 19 * 9 + 18, ("q4_0", False): 10, ("q4_0", True): 10,
            # IQ lattice searches, counted on the benchmark distribution (off-grid problems and
            # neighbour-list lengths from an instrumented run): candidates per value x (4 ops per
            # position + 1 compare) + sweep steps x 12 (levels, accept sums) + 15 (weights,
