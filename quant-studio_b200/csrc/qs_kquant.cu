@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
     __shared__ __align__(16) float s_sq[SBT * QK_K];  // squares, then the SB's level bytes
     __shared__ float s_part[SBT][8];
     __shared__ float s_sc[SBT][NG], s_mn[SBT][NG], s_sw[SBT][NG], s_ls[SBT][NG], s_lm[SBT][NG];
-    __shared__ float s_d[SBT], s_m[SBT];
+    __shared__ float s_mse[SBT][18];
     __shared__ __align__(16) uint8_t s_out[SBT * BB];
 
     const int tid = threadIdx.x, sbl = tid / NG, g = tid % NG;
@@ -237,23 +237,14 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
         uint16_t d16, m16;
         int ls, lm;  // this group's 8-bit codes
         if (IMAT) {
-            if (g < 2) {
-                float v[NG], sw[NG], lv[NG];
-#pragma unroll
-                for (int j = 0; j < NG; j++) {
-                    v[j] = g == 0 ? s_sc[sbl][j] : s_mn[sbl][j];
-                    sw[j] = s_sw[sbl][j];
-                }
-                const float dd = qp_search<NG>(v, sw, (float)Tr::QPMAX, s_qp, lv);
-#pragma unroll
-                for (int j = 0; j < NG; j++) (g == 0 ? s_ls : s_lm)[sbl][j] = lv[j];
-                (g == 0 ? s_d : s_m)[sbl] = dd;
-            }
-            __syncwarp();
-            d16 = f16_bits(s_d[sbl]);
-            m16 = f16_bits(s_m[sbl]);
-            ls = (int)((long long)s_ls[sbl][g] & 0xFF);
-            lm = (int)((long long)s_lm[sbl][g] & 0xFF);
+            float La, Lb, da, db;
+            qp_pair<NG>(s_sc[sbl], s_mn[sbl], s_sw[sbl], (float)Tr::QPMAX, s_qp, s_mse[sbl], g, La, Lb, da, db);
+            s_ls[sbl][g] = La;
+            s_lm[sbl][g] = Lb;
+            d16 = f16_bits(da);
+            m16 = f16_bits(db);
+            ls = (int)((long long)La & 0xFF);
+            lm = (int)((long long)Lb & 0xFF);
         } else {
             float max_scale = s_sc[sbl][0], max_min = s_mn[sbl][0];
 #pragma unroll

@@ -144,6 +144,139 @@ __device__ __forceinline__ float qp_search(const float* x, const float* w, float
     return scale;
 }
 
+// One element's greedy try of make_qp_quants_eager (kernels/kq_common.py:125-137) against the
+// superblock's current sums, for qp_pair below. State is replicated on the superblock's
+// lanes except L (the lane's own level). The first lane at or after the pass position whose
+// element commits is applied: the elements before it were tried with the same sums and did
+// not commit, exactly as in the sequential pass.
+struct QpGreedy {
+    float slx, sl2, L;
+    int pos, pass;
+    bool moved, done;
+};
+
+template <int N>
+__device__ __forceinline__ void qp_greedy_try(QpGreedy& st, float xi, float wi, float nmax, int g, int base) {
+    const float Li = st.L;
+    const float slx = st.slx - (wi * xi) * Li;
+    const float sl2 = st.sl2 - (wi * Li) * Li;
+    const bool ok = slx > 0.0f && sl2 > 0.0f;
+    const float newl = min_hi(rintf(__fdiv_rn(xi * sl2, ok ? slx : 1.0f)), nmax);
+    const float slx2 = slx + (wi * xi) * newl;
+    const float sl22 = sl2 + (wi * newl) * newl;
+    const bool commit = !st.done && g >= st.pos && ok && newl != Li &&
+                        (slx2 * slx2) * st.sl2 > (st.slx * st.slx) * sl22;
+    const unsigned bits = (__ballot_sync(0xFFFFFFFFu, commit) >> base) & ((1u << N) - 1u);
+    const int j = bits ? __ffs(bits) - 1 : g;
+    const float nx = __shfl_sync(0xFFFFFFFFu, slx2, base + j);
+    const float n2 = __shfl_sync(0xFFFFFFFFu, sl22, base + j);
+    if (st.done) return;
+    if (bits) {
+        st.slx = nx;
+        st.sl2 = n2;
+        if (g == j) st.L = newl;
+        st.moved = true;
+        st.pos = j + 1;
+    } else {
+        st.pos = N;
+    }
+    if (st.pos == N) {  // end of the pass; a pass without a commit would repeat unchanged
+        if (!st.moved || st.pass == 4) st.done = true;
+        else { st.pass++; st.pos = 0; st.moved = false; }
+    }
+}
+
+// make_qp_quants_eager (kernels/kq_common.py:99-141) for both vectors of one superblock (its
+// N block scales xa and N block mins xb, weights w; all in shared memory), spread over the
+// superblock's N lanes (N = 8 or 16, lanes aligned to N in the warp; every lane of the warp
+// calls this). Lane g owns element g. The 18 candidate fits (first guess + 8 steps, per
+// vector) are evaluated one per lane per round into mse[18]; every lane replays the strict-<
+// selection over them in the reference's order; the greedy passes run element-parallel
+// (qp_greedy_try). Results: the lane's own levels La / Lb and the scales da / db, the same
+// values qp_search gives for each vector.
+template <int N>
+__device__ __forceinline__ void qp_pair(const float* xa, const float* xb, const float* w, float nmax,
+                                        const float* steps, float* mse, int g,
+                                        float& La, float& Lb, float& da, float& db) {
+    const int base = (threadIdx.x & 31) & ~(N - 1);
+    float mxa = xa[0], mxb = xb[0];
+#pragma unroll
+    for (int i = 1; i < N; i++) {
+        mxa = xa[i] > mxa ? xa[i] : mxa;
+        mxb = xb[i] > mxb ? xb[i] : mxb;
+    }
+    const bool deada = mxa < EPS15, deadb = mxb < EPS15;
+    const float ra = rcp_rn(deada ? 1.0f : mxa), rb = rcp_rn(deadb ? 1.0f : mxb);
+
+#pragma unroll 1
+    for (int j = g; j < 18; j += N) {
+        const bool vb = j >= 9;
+        const int c = vb ? j - 9 : j;
+        const float* x = vb ? xb : xa;
+        const float isc = (vb ? rb : ra) * (c == 0 ? nmax : steps[c - 1]);
+        const float ric = rcp_rn(isc);
+        const float hi = c == 0 ? __int_as_float(0x7F800000) : nmax;  // the first guess is not clamped
+        float s = 0.0f;
+        if (N == 8) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float d = x[i] - ric * min_hi(rintf(isc * x[i]), hi);
+                s = __fadd_rn(s, w[i] * (d * d));
+            }
+        } else {
+#pragma unroll
+            for (int l = 0; l < 8; l++) {
+                const float d0 = x[l] - ric * min_hi(rintf(isc * x[l]), hi);
+                const float d1 = x[8 + l] - ric * min_hi(rintf(isc * x[8 + l]), hi);
+                s = __fadd_rn(s, __fadd_rn(w[l] * (d0 * d0), w[8 + l] * (d1 * d1)));
+            }
+        }
+        mse[j] = s;
+    }
+    __syncwarp();
+
+    float isa = ra * nmax, isb = rb * nmax, ba = mse[0], bb = mse[9];
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+        if (mse[1 + s] < ba) { ba = mse[1 + s]; isa = ra * steps[s]; }
+        if (mse[10 + s] < bb) { bb = mse[10 + s]; isb = rb * steps[s]; }
+    }
+    QpGreedy A{0.0f, 0.0f, 0.0f, 0, 0, false, false}, B{0.0f, 0.0f, 0.0f, 0, 0, false, false};
+    {
+        float t[N], u[N];
+#pragma unroll
+        for (int i = 0; i < N; i++) {
+            const float l = min_hi(rintf(isa * xa[i]), nmax);
+            t[i] = (w[i] * xa[i]) * l;
+            u[i] = (w[i] * l) * l;
+        }
+        A.slx = torch_sum<N>(t);
+        A.sl2 = torch_sum<N>(u);
+#pragma unroll
+        for (int i = 0; i < N; i++) {
+            const float l = min_hi(rintf(isb * xb[i]), nmax);
+            t[i] = (w[i] * xb[i]) * l;
+            u[i] = (w[i] * l) * l;
+        }
+        B.slx = torch_sum<N>(t);
+        B.sl2 = torch_sum<N>(u);
+    }
+    const float xga = xa[g], xgb = xb[g], wg = w[g];
+    A.L = min_hi(rintf(isa * xga), nmax);
+    B.L = min_hi(rintf(isb * xgb), nmax);
+#pragma unroll 1
+    while (__any_sync(0xFFFFFFFFu, !(A.done && B.done))) {
+        qp_greedy_try<N>(A, xga, wg, nmax, g, base);
+        qp_greedy_try<N>(B, xgb, wg, nmax, g, base);
+    }
+    da = A.sl2 > 0.0f ? __fdiv_rn(A.slx, A.sl2 < F32_TINY ? F32_TINY : A.sl2) : 0.0f;
+    db = B.sl2 > 0.0f ? __fdiv_rn(B.slx, B.sl2 < F32_TINY ? F32_TINY : B.sl2) : 0.0f;
+    La = deada ? 0.0f : A.L;
+    Lb = deadb ? 0.0f : B.L;
+    if (deada) da = 0.0f;
+    if (deadb) db = 0.0f;
+}
+
 // make_qx_quants_eager (kernels/qx_common.py:52-82), rmse_type 1; L gets level + NMAX.
 // steps: the 18 candidate numerators.
 template <int N>
