@@ -72,6 +72,14 @@ __device__ __forceinline__ void load_f32(const float* p, float* v) {
 __device__ __forceinline__ float rcp_rn(float x) { return __fdiv_rn(1.0f, x); }
 __device__ __forceinline__ float clampf(float x, float lo, float hi) { return x < lo ? lo : (x > hi ? hi : x); }
 __device__ __forceinline__ float min_hi(float x, float hi) { return x > hi ? hi : x; }
+// clampf for the search loops, two NaN-propagating min/max instructions: equal to clampf for
+// every non-NaN x (a -0 may come out +0, which only reaches an all-zero level sum, where the
+// candidate is rejected anyway) and NaN for NaN x, so every accept decision is the same.
+__device__ __forceinline__ float clamp_nan(float x, float lo, float hi) {
+    float r;
+    asm("{.reg .f32 t; max.NaN.f32 t, %1, %2; min.NaN.f32 %0, t, %3;}" : "=f"(r) : "f"(x), "f"(lo), "f"(hi));
+    return r;
+}
 __device__ __forceinline__ uint16_t f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
 __device__ __forceinline__ float f16_val(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 

@@ -29,7 +29,7 @@ __device__ __forceinline__ float qkx_search(const float* x, const float* w, cons
     float scale = rcp_rn(iscale);
 #pragma unroll
     for (int i = 0; i < N; i++) {
-        float l = clampf(rintf(iscale * (x[i] - mn)), 0.0f, fmax);
+        float l = clamp_nan(rintf(iscale * (x[i] - mn)), 0.0f, fmax);
         float d = (scale * l + mn) - x[i];
         t[i] = MAD ? w[i] * fabsf(d) : w[i] * (d * d);
     }
@@ -43,7 +43,7 @@ __device__ __forceinline__ float qkx_search(const float* x, const float* w, cons
         float la[N], wl[N], wl2[N], wlx[N];
 #pragma unroll
         for (int i = 0; i < N; i++) {
-            la[i] = clampf(rintf(isc * (x[i] - mn)), 0.0f, fmax);
+            la[i] = clamp_nan(rintf(isc * (x[i] - mn)), 0.0f, fmax);
             wl[i] = w[i] * la[i];
             wl2[i] = wl[i] * la[i];
             wlx[i] = wl[i] * x[i];
