@@ -448,6 +448,9 @@ def bench_cli(args) -> None:
             raise SystemExit(f"CLI failed ({r.returncode}): {r.stderr[-2000:]}")
         m = re.search(r"done in ([0-9.]+)s", r.stdout)
         phases = dict((k, float(v)) for k, v in re.findall(r"(\w+) ([0-9.]+)", r.stdout.split("pipeline seconds", 1)[-1].split("\n", 1)[0].split(":", 1)[-1]))
+        w = re.search(r"waited ([0-9.]+)s for device start-up", r.stdout)
+        if w:
+            phases["startup_wait"] = float(w.group(1))
         if i >= args.warmup:
             runs.append((float(m.group(1)), wall, phases))
     q_s = statistics.median(x for x, _, _ in runs)

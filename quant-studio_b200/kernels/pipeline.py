@@ -86,6 +86,33 @@ class _Slot:
         return buf
 
 
+# Staging slots allocated ahead of a run, per device index (stage_buffers); taken by _open.
+_STAGED: dict[int, list[_Slot]] = {}
+_STAGED_LOCK = threading.Lock()
+
+
+def _fill_slot(sl: _Slot, device: torch.device, in_bytes: int, out_bytes: int, max_k: int) -> None:
+    sl.h_in = _Slot._grow_pinned(sl.h_in, in_bytes)
+    sl.h_out = _Slot._grow_pinned(sl.h_out, out_bytes)
+    sl.d_in = _Slot._grow_dev(sl.d_in, in_bytes, device)
+    sl.d_out = _Slot._grow_dev(sl.d_out, out_bytes, device)
+    if sl.h_qw is None or sl.h_qw.numel() < max_k:
+        sl.h_qw = torch.empty(max(max_k, 1), dtype=torch.float32, pin_memory=True)
+        sl.d_qw = torch.empty(max(max_k, 1), dtype=torch.float32, device=device)
+
+
+def stage_buffers(device: torch.device, in_bytes: int, out_bytes: int, max_k: int = 1 << 16) -> None:
+    """Allocate one device's staging slots (pinned and device buffers, streams) ahead of a
+    run, e.g. on a start-up thread while the model is read and planned. The next
+    ShardedQuantizer that opens this device takes them and only grows what is too small."""
+    torch.cuda.set_device(device)
+    slots = [_Slot(device), _Slot(device)]
+    for sl in slots:
+        _fill_slot(sl, device, in_bytes, out_bytes, max_k)
+    with _STAGED_LOCK:
+        _STAGED[device.index] = slots
+
+
 class ShardedQuantizer:
     """Quantize a list of jobs across `devices`, writing into the open file `fd`."""
 
@@ -154,15 +181,13 @@ class ShardedQuantizer:
     # -- one GPU -----------------------------------------------------------
     def _open(self, device: torch.device):
         torch.cuda.set_device(device)
-        slots = [_Slot(device), _Slot(device)]
         t0 = time.perf_counter()
+        with _STAGED_LOCK:
+            slots = _STAGED.pop(device.index, None)
+        if slots is None:
+            slots = [_Slot(device), _Slot(device)]
         for sl in slots:  # sized once for the largest chunk of the run
-            sl.h_in = _Slot._grow_pinned(None, self._max_in)
-            sl.h_out = _Slot._grow_pinned(None, self._max_out)
-            sl.d_in = _Slot._grow_dev(None, self._max_in, device)
-            sl.d_out = _Slot._grow_dev(None, self._max_out, device)
-            sl.h_qw = torch.empty(max(self._max_k, 1), dtype=torch.float32, pin_memory=True)
-            sl.d_qw = torch.empty(max(self._max_k, 1), dtype=torch.float32, device=device)
+            _fill_slot(sl, device, self._max_in, self._max_out, self._max_k)
         self._tick("alloc", t0)
         return {"device": device, "slots": slots, "next": 0}
 

@@ -31,7 +31,7 @@ from gguf import GGMLQuantizationType, GGUFReader, GGUFValueType, GGUFWriter
 from gguf.constants import GGML_QUANT_SIZES, GGML_QUANT_VERSION
 
 from kernels import QUANT_TYPES, TORCH_DTYPES, _native, scheme
-from kernels.pipeline import CopyJob, QuantJob, ShardedQuantizer
+from kernels.pipeline import CopyJob, QuantJob, ShardedQuantizer, stage_buffers
 
 
 def parse_mem(s: str) -> int:
@@ -112,17 +112,23 @@ def pick_devices(device: str, ngpus: int) -> list[torch.device]:
 
 
 def start_device_warmup(args) -> tuple[threading.Thread, dict]:
-    """Pick the devices and bring up their CUDA contexts and libqsb200 state on a background
-    thread, while the main thread reads and plans the model."""
+    """Pick the devices, bring up their CUDA contexts and libqsb200 state and allocate the
+    pipeline's staging buffers on a background thread, while the main thread reads and plans
+    the model."""
     box: dict = {}
 
     def run() -> None:
         try:
             devs = pick_devices(args.device, args.gpus)
+            # a chunk holds at most CHUNK_BYTES of source rows; blocks are under half of that
+            # from 16-bit sources (the pipeline grows the staging if a run needs more)
+            in_bytes = min(ShardedQuantizer.CHUNK_BYTES, 16 * parse_mem(args.mem))
             for d in devs:
                 torch.cuda.set_device(d)
                 torch.empty(1, device=d)
                 _native.check(_native.lib().qs_init(d.index))
+            for d in devs:
+                stage_buffers(d, in_bytes, in_bytes // 2)
             box["devices"] = devs
         except BaseException as e:  # re-raised on the main thread
             box["error"] = e
@@ -262,11 +268,14 @@ def main() -> None:
         print(f"dry run: {fmt_size(tin)} -> {fmt_size(tout)} tensor data ({tout / max(tin, 1) * 100:.1f}%)")
         return
 
+    t_wait = time.perf_counter()
     warm[0].join()
+    t_wait = time.perf_counter() - t_wait
     if "error" in warm[1]:
         raise warm[1]["error"]
     devices = warm[1]["devices"]
-    print(f"qs-b200: {args.input} -> {out_path} [{opt.name}] gpus={len(devices)} mem={args.mem}")
+    print(f"qs-b200: {args.input} -> {out_path} [{opt.name}] gpus={len(devices)} mem={args.mem} "
+          f"(waited {t_wait:.3f}s for device start-up)")
     if args.imatrix is not None:
         print(f"imatrix: {len(imatrix)} entries from {args.imatrix}")
 
