@@ -469,15 +469,18 @@ def bench_cli(args) -> None:
 
 def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, world, n_elem):
     """Host-buffer pipeline: chunks of rows go H2D on one stream, are quantized and copied
-    back on another; events order the two so copies overlap the kernels."""
-    chunk_rows = 2048
+    back on another; events order the two so copies overlap the kernels. Chunks of 64 MB of
+    source rows: measured on a B200 over PCIe, 16 / 32 / 64 / 112 MB chunks reached 46 / 49 /
+    52 / 46 GB/s against 55.6 GB/s for a lone pinned H2D copy (about 48.5 per direction with
+    the blocks copied back at the same time)."""
+    kmax = max(x.shape[1] for x in xs)
+    chunk_rows = max(1, (64 << 20) // (kmax * xs[0].element_size()))
     h_in = [torch.empty(x.shape, dtype=x.dtype, pin_memory=True) for x in xs]
     for h, x in zip(h_in, xs):
         h.copy_(x)
     h_out = [torch.empty(o.shape, dtype=torch.uint8, pin_memory=True) for o in outs]
     s_h2d, s_comp, s_d2h = (torch.cuda.Stream(device) for _ in range(3))
     nbuf = 3
-    kmax = max(x.shape[1] for x in xs)
     d_in = [torch.empty((chunk_rows, kmax), dtype=torch.bfloat16, device=device) for _ in range(nbuf)]
     d_out = [torch.empty((chunk_rows, max(o.shape[1] for o in outs)), dtype=torch.uint8, device=device)
              for _ in range(nbuf)]
