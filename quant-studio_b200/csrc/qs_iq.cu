@@ -464,7 +464,14 @@ __device__ void iq_flush(IqWarpSmem<Tr>& W, const IqGridDev& G, int lane) {
             take(iq_dist<Tr::NPOS, true>(tb, v0.x, lb), v0.x >> 16);
             take(iq_dist<Tr::NPOS, false>(tb, v0.y, lb), v0.y & 0xFFFF);
             take(iq_dist<Tr::NPOS, true>(tb, v0.y, lb), v0.y >> 16);
-            for (int c = 1; c < n; c++) quad(__ldg(lp + c));
+            // quads are requested two iterations ahead of their use
+            uint2 nx1 = n > 1 ? __ldg(lp + 1) : v0, nx2 = n > 2 ? __ldg(lp + 2) : v0;
+            for (int c = 1; c < n; c++) {
+                const uint2 cur = nx1;
+                nx1 = nx2;
+                if (c + 2 < n) nx2 = __ldg(lp + c + 2);
+                quad(cur);
+            }
             W.win[g][(slot == IQ_FINAL ? 0 : slot) * Tr::NSUB + q] = bc | IQ_SEARCHED;
         }
     }
