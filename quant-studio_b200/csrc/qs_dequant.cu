@@ -496,10 +496,10 @@ namespace {
 
 // Per-CTA partial sums (weighted, plain) of one launch. Every CTA of the launch writes its
 // own pair before the final pass reads the pairs, so nothing here needs to start at zero.
-__device__ __align__(256) double g_na_partial[2 * NA_MAX_PARTIALS];
+static __device__ __align__(256) double g_na_partial[2 * NA_MAX_PARTIALS];
 // The five IQ codebooks (grid index -> code), copied in once per device at set-up.
 constexpr int NA_KG_OFF[5] = {0, 256, 768, 1792, 2048};
-__device__ __align__(256) uint16_t g_na_kgrid[256 + 512 + 1024 + 256 + 512];
+static __device__ __align__(256) uint16_t g_na_kgrid[256 + 512 + 1024 + 256 + 512];
 
 std::mutex g_na_mu;
 NoAllocDevice g_na_dev[NA_MAX_DEVICES];
