@@ -56,3 +56,30 @@ def test_weights_stay_alive_across_jobs(qtype, tmp_path):
         bad = np.nonzero((got != w).any(1))[0]
         assert bad.size == 0, f"{j.name}: {bad.size} rows differ, first {bad[:8]}"
         off += w.size
+
+
+def test_staged_buffers_taken_over_and_grown(tmp_path):
+    """Staging allocated ahead of a run (as the CLI's start-up thread does) is taken over by
+    the run, grown where the run's chunks are larger, and left staged for no later run."""
+    from kernels import pipeline
+
+    dev = torch.device("cuda", 0)
+    pipeline.stage_buffers(dev, in_bytes=1 << 16, out_bytes=1 << 15, max_k=256)  # deliberately small
+    assert 0 in pipeline._STAGED
+    rng = np.random.default_rng(11)
+    k, rows = 2048, 512
+    raw, xf = _bf16_rows(rng, rows, k)
+    qw = rng.lognormal(0.0, 1.5, k).astype(np.float32)
+    gt = oracle.TYPE_IDS["q4_k"]
+    rb = _native.row_bytes(gt, k)
+    job = QuantJob("t", raw, torch.bfloat16, k, gt, qw, 0, rb, 5)
+    path = tmp_path / "out.bin"
+    fd = os.open(path, os.O_RDWR | os.O_CREAT, 0o644)
+    try:
+        os.ftruncate(fd, rows * rb)
+        ShardedQuantizer([dev], fd, mem_bytes=4 << 30).run([job])
+    finally:
+        os.close(fd)
+    assert 0 not in pipeline._STAGED
+    got = np.fromfile(path, dtype=np.uint8).reshape(rows, rb)
+    assert np.array_equal(got, oracle.quantize("q4_k", xf, qw))
