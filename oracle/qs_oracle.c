@@ -214,7 +214,7 @@ static f32 make_q3(const f32 *x, int n, int nmax, f32 *L) {
 static f32 make_qkx(const f32 *x, const f32 *w, int n, const f32 *steps, int nsteps, int nmax,
                     int use_mad, f32 *the_min, f32 *L) {
     const f32 fmax = (f32)nmax;
-    f32 t[32], La[32];
+    f32 t[32] = {0}, La[32];  /* zeroed: only t[0..n) is read, gcc cannot see that */
     f32 mn = minv(x, n);
     mn = mn > 0.0f ? 0.0f : mn;
     f32 mx = maxv(x, n);
