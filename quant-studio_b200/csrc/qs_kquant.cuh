@@ -190,7 +190,7 @@ __device__ __forceinline__ void qp_greedy_try(QpGreedy& st, float xi, float wi, 
 // N block scales xa and N block mins xb, weights w; all in shared memory), spread over the
 // superblock's N lanes (N = 8 or 16, lanes aligned to N in the warp; every lane of the warp
 // calls this). Lane g owns element g. The 18 candidate fits (first guess + 8 steps, per
-// vector) are evaluated one per lane per round into mse[18]; every lane replays the strict-<
+// vector) are evaluated one per lane per pass into mse[18]; every lane replays the strict-<
 // selection over them in the reference's order; the greedy passes run element-parallel
 // (qp_greedy_try). Results: the lane's own levels La / Lb and the scales da / db, the same
 // values qp_search gives for each vector.
