@@ -17,7 +17,7 @@ only for the barrier and the max-over-ranks of the timings).
          row chunks with the copies and kernels overlapped on three streams
   roofline  the Q4_K kernel against the FP32 lane-op ceiling (148 SMs x 128 lanes x SM clock):
          algorithmic ops = 655 per value (37 x 17 per candidate step + 11 initial + 3 sums
-         + 5 weights + 7 requant/pack), see DESIGN.md; plus the HBM view of the same launches
+         + 5 weights + 7 requant/pack); plus the HBM view of the same launches
 cpu_baseline  the CPU restatement of the reference's algorithm (oracle/) on all host cores over
          a bounded sample of the workload; the same sample is quantized on the GPU and
          `identical_blocks` is the fraction of blocks that match (the metric's identical-block %)

@@ -13,6 +13,11 @@
  * Type ids are gguf GGMLQuantizationType values; source types are GGML F32 (0),
  * F16 (1) and BF16 (30). Every function returns QS_OK (0) or a negative QS_E* code;
  * qs_last_error() gives the message of the calling thread's last failure.
+ *
+ * Devices: a call runs on the GPU that owns its first device pointer (src, or out for the
+ * tensor error sums), whatever device the caller has current; every other pointer of the
+ * call must be memory of that same GPU (or managed memory), else QS_EINVAL. The calling
+ * thread's current CUDA context is the same on return as it was on entry.
  */
 #ifndef QSB200_H
 #define QSB200_H
@@ -120,7 +125,7 @@ int qs_block_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes, 
 /*
  * Error sums over the whole tensor (terms and 8-value runs as qs_block_error), the runs
  * added in double in a fixed order (the same bits on every call on the same GPU model):
- *   out[0] = sum w * (deq - x)^2, out[1] = sum (deq - x)^2   (out: 2 device doubles)
+ *   out[0] = sum w * (deq - x)^2, out[1] = sum (deq - x)^2   (out: 2 device doubles, 8-byte aligned)
  * out[1] / (n_rows * k) is the `((dq - xf) ** 2).mean()` of tools/dev_harness.py:110-111.
  * Arguments as qs_block_error. Scratch for the per-CTA partial sums comes from the
  * library's per-device memory pool, stream-ordered on `stream` (cudaMallocFromPoolAsync /
@@ -148,7 +153,8 @@ int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes,
  * scratch and race; callers must serialize them.
  * Set-up: the first call on each device, with that device current, resolves the static
  * arrays (cudaGetSymbolAddress) and copies the codebooks in (a synchronous copy); make
- * that first call outside any stream capture.
+ * that first call outside any stream capture. Like every entry point here, the call
+ * leaves the caller's current context as it found it.
  */
 int qs_tensor_error_noalloc(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x,
                             int x_type, int64_t n_rows, int64_t k, const float* qw, double* out, void* stream);

@@ -1,5 +1,6 @@
 // C ABI of libqsb200 (declared in include/qsb200.h): argument checks, per-device
 // state, dispatch to the kernel files.
+#include <cuda.h>  // CUcontext (the driver calls themselves are resolved at run time)
 #include <mutex>
 #include <stdarg.h>
 #include <stdio.h>
@@ -81,6 +82,65 @@ int ensure_device(int device, DeviceState** out) {
     return QS_OK;
 }
 
+// The calling thread's current CUDA context, saved when an entry point starts and put back
+// when it returns: a call that runs on the device owning its data (cudaSetDevice) must not
+// leave that device current for the caller, nor create a context the caller never had.
+// The two driver calls are looked up once through the runtime, so the library does not
+// link libcuda directly.
+struct CtxFns {
+    CUresult (*get)(CUcontext*) = nullptr;
+    CUresult (*set)(CUcontext) = nullptr;
+};
+
+const CtxFns& ctx_fns() {
+    static CtxFns f;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* g = nullptr;
+        void* s = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &g, cudaEnableDefault, &q1) == cudaSuccess &&
+            cudaGetDriverEntryPoint("cuCtxSetCurrent", &s, cudaEnableDefault, &q2) == cudaSuccess &&
+            q1 == cudaDriverEntryPointSuccess && q2 == cudaDriverEntryPointSuccess) {
+            f.get = reinterpret_cast<CUresult (*)(CUcontext*)>(g);
+            f.set = reinterpret_cast<CUresult (*)(CUcontext)>(s);
+        }
+    });
+    return f;
+}
+
+class CurrentContextGuard {
+public:
+    CurrentContextGuard() {
+        const CtxFns& f = ctx_fns();
+        ok_ = f.get && f.get(&saved_) == CUDA_SUCCESS;
+    }
+    ~CurrentContextGuard() {
+        if (!ok_) return;
+        const CtxFns& f = ctx_fns();
+        CUcontext now = nullptr;
+        if (f.get(&now) == CUDA_SUCCESS && now != saved_) f.set(saved_);
+    }
+    CurrentContextGuard(const CurrentContextGuard&) = delete;
+    CurrentContextGuard& operator=(const CurrentContextGuard&) = delete;
+
+private:
+    CUcontext saved_ = nullptr;
+    bool ok_ = false;
+};
+
+// `p` must be memory of `device` (or managed memory): a pointer into another GPU's memory
+// would otherwise reach the kernel and fault there.
+int check_on_device(const void* p, int device, const char* what) {
+    cudaPointerAttributes pa;
+    cudaError_t e = cudaPointerGetAttributes(&pa, p);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+    if (pa.type == cudaMemoryTypeManaged) return QS_OK;
+    if (pa.type != cudaMemoryTypeDevice) return fail(QS_EINVAL, "%s is not device memory", what);
+    if (pa.device != device) return fail(QS_EINVAL, "%s is on device %d, the call runs on device %d", what, pa.device, device);
+    return QS_OK;
+}
+
 }  // namespace
 
 #define QS_API __attribute__((visibility("default")))
@@ -115,14 +175,11 @@ QS_API int qs_row_bytes(int ggml_type, int64_t k, int64_t* out_bytes) {
 }
 
 QS_API int qs_init(int device) {
-    int prev = -1;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-    if (prev != device && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    CurrentContextGuard keep;
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
     DeviceState* d = nullptr;
-    int rc = ensure_device(device, &d);
-    if (prev != device) cudaSetDevice(prev);
-    return rc;
+    return ensure_device(device, &d);
 }
 
 }  // extern "C"
@@ -189,6 +246,7 @@ QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_r
     if (!src || !dst) return fail(QS_EINVAL, "null src or dst");
     if (((uintptr_t)src & 15) || (qw && ((uintptr_t)qw & 15)))
         return fail(QS_EINVAL, "src and qw must be 16-byte aligned");
+    CurrentContextGuard keep;
 
     // run on the device that owns src (the runtime's current device may belong to another
     // runtime instance in the process, e.g. the one torch links)
@@ -201,9 +259,10 @@ QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_r
     int cur = -1;
     if ((e = cudaGetDevice(&cur)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (cur != device && (e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    int rc;
+    if ((rc = check_on_device(dst, device, "dst")) || (qw && (rc = check_on_device(qw, device, "qw")))) return rc;
     DeviceState* d = nullptr;
-    int rc = ensure_device(device, &d);
-    if (rc) return rc;
+    if ((rc = ensure_device(device, &d))) return rc;
 
     qs::QuantArgs a;
     a.src = src;
@@ -233,9 +292,11 @@ QS_API int qs_dequantize(int ggml_type, const void* src, int64_t src_row_bytes, 
     if (n_rows == 0) return QS_OK;
     if (!src || !dst) return fail(QS_EINVAL, "null src or dst");
     if ((uintptr_t)dst & 15) return fail(QS_EINVAL, "dst must be 16-byte aligned");
+    CurrentContextGuard keep;
     int device;
     DeviceState* d;
     if ((rc = device_of(src, "src", &device, &d))) return rc;
+    if ((rc = check_on_device(dst, device, "dst"))) return rc;
     c.dst = dst;
     c.dst_stride = dst_row_stride;
     qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
@@ -251,9 +312,14 @@ QS_API int qs_block_error(int ggml_type, const void* blocks, int64_t blocks_row_
     if (n_rows == 0) return QS_OK;
     if ((rc = check_source(x, x_type, qw))) return rc;
     if (!blocks || !err) return fail(QS_EINVAL, "null blocks or err");
+    if ((uintptr_t)err & 7) return fail(QS_EINVAL, "err must be 8-byte aligned");
+    CurrentContextGuard keep;
     int device;
     DeviceState* d;
     if ((rc = device_of(blocks, "blocks", &device, &d))) return rc;
+    if ((rc = check_on_device(x, device, "x")) || (qw && (rc = check_on_device(qw, device, "qw"))) ||
+        (rc = check_on_device(err, device, "err")))
+        return rc;
     c.x = x;
     c.x_type = x_type;
     c.qw = qw;
@@ -269,13 +335,18 @@ QS_API int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row
     int rc = check_decode(ggml_type, blocks, blocks_row_bytes, n_rows, k, c);
     if (rc) return rc;
     if (!out) return fail(QS_EINVAL, "null out");
+    if ((uintptr_t)out & 7) return fail(QS_EINVAL, "out must be 8-byte aligned");
     if (n_rows > 0) {
         if ((rc = check_source(x, x_type, qw))) return rc;
         if (!blocks) return fail(QS_EINVAL, "null blocks");
     }
+    CurrentContextGuard keep;
     int device;
     DeviceState* d;
     if ((rc = device_of(out, "out", &device, &d))) return rc;
+    if (n_rows > 0 && ((rc = check_on_device(blocks, device, "blocks")) || (rc = check_on_device(x, device, "x")) ||
+                       (qw && (rc = check_on_device(qw, device, "qw")))))
+        return rc;
     c.x = x;
     c.x_type = x_type;
     c.qw = qw;
@@ -301,10 +372,12 @@ QS_API int qs_tensor_error_noalloc(int ggml_type, const void* blocks, int64_t bl
     int rc = check_decode(ggml_type, blocks, blocks_row_bytes, n_rows, k, c);
     if (rc) return rc;
     if (!out) return fail(QS_EINVAL, "null out");
+    if ((uintptr_t)out & 7) return fail(QS_EINVAL, "out must be 8-byte aligned");
     if (n_rows > 0) {
         if ((rc = check_source(x, x_type, qw))) return rc;
         if (!blocks) return fail(QS_EINVAL, "null blocks");
     }
+    CurrentContextGuard keep;
     cudaPointerAttributes pa;
     cudaError_t e = cudaPointerGetAttributes(&pa, out);
     if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
@@ -312,6 +385,9 @@ QS_API int qs_tensor_error_noalloc(int ggml_type, const void* blocks, int64_t bl
     int cur = -1;
     if ((e = cudaGetDevice(&cur)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (cur != pa.device && (e = cudaSetDevice(pa.device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    if (n_rows > 0 && ((rc = check_on_device(blocks, pa.device, "blocks")) || (rc = check_on_device(x, pa.device, "x")) ||
+                       (qw && (rc = check_on_device(qw, pa.device, "qw")))))
+        return rc;
     const qs::NoAllocDevice* d = nullptr;
     if ((e = qs::noalloc_setup(pa.device, &d)) != cudaSuccess) return cuda_fail(e, "static scratch set-up");
     c.x = x;

@@ -30,13 +30,18 @@ TYPES = {
 
 
 def quantizer(name: str):
-    """quantize_<name>(x, qw=None): x (n, k) f32/f16/bf16 on a CUDA device -> new uint8 rows."""
+    """quantize_<name>(x, qw=None): x (n, k) f32/f16/bf16 on a CUDA device -> new uint8 rows.
+
+    The reference's quantize_iq2_xxs also takes `T`, its host-side table cache
+    (kernels/iq2.py:418); it is accepted and ignored here, since the lattice tables live on
+    each device inside libqsb200."""
     gt = TYPES[name][0]
 
-    def fn(x, qw=None):
+    def fn(x, qw=None, T=None):
         return _native.quantize(int(gt), x, qw)
 
     fn.__name__ = f"quantize_{name}"
+    fn.__qualname__ = fn.__name__
     fn.__doc__ = (f"x: (n_rows, k) float32/float16/bfloat16 CUDA tensor; qw: (k,) float32 importance "
                   f"weights or None. Returns (n_rows, k // QK * block_bytes) uint8 on x's device.")
     return fn

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import argparse
 import os
+import re
 import sys
 import threading
 import time
@@ -34,41 +35,52 @@ from kernels import QUANT_TYPES, TORCH_DTYPES, _native, scheme
 from kernels.pipeline import CopyJob, QuantJob, ShardedQuantizer, stage_buffers
 
 
-def parse_mem(s: str) -> int:
-    s = s.strip().upper()
-    units = {"K": 1 << 10, "M": 1 << 20, "G": 1 << 30}
-    if s and s[-1] in units:
-        return int(float(s[:-1]) * units[s[-1]])
-    return int(s)
+_MEM_RE = re.compile(r"(\d+(?:\.\d*)?|\.\d+)\s*([KMG]?)(?:I?B)?", re.IGNORECASE)
+_MEM_SHIFT = {"": 0, "K": 10, "M": 20, "G": 30}
 
 
-def parse_ggml_type(s: str) -> GGMLQuantizationType:
-    try:
-        return GGMLQuantizationType[s.upper()]
-    except KeyError:
-        sys.exit(f"error: unknown ggml type: {s}")
+def parse_mem(text: str) -> int:
+    """--mem value in bytes: a number with an optional binary K / M / G suffix ("4G",
+    "512m", "1.5G", "65536"); the reference's --mem accepts the same forms
+    (quant-studio.py:41-48). A trailing "B" / "iB" is tolerated."""
+    m = _MEM_RE.fullmatch(text.strip())
+    if m is None:
+        sys.exit(f"error: --mem {text!r} is not a size like 4G, 512M or 65536")
+    return int(float(m.group(1)) * (1 << _MEM_SHIFT[m.group(2).upper()]))
+
+
+_GGML_TYPE_BY_NAME = {t.name.lower(): t for t in GGMLQuantizationType}
+
+
+def parse_ggml_type(text: str) -> GGMLQuantizationType:
+    """A ggml type name in any case (q4_0, Q6_K, bf16) as --token-embedding-type,
+    --output-tensor-type and --tensor-type take it."""
+    t = _GGML_TYPE_BY_NAME.get(text.strip().lower())
+    if t is None:
+        sys.exit(f"error: unknown ggml type: {text}")
+    return t
 
 
 def load_imatrix(path: Path) -> dict[str, np.ndarray]:
-    """Per tensor: mean squared input activation per column, in_sum2 / counts (0 where
-    the count is 0), like the reference's load_imatrix (quant-studio.py:68-87)."""
-    r = GGUFReader(path)
-    sums, counts = {}, {}
-    for t in r.tensors:
-        if t.name.endswith(".in_sum2"):
-            sums[t.name[: -len(".in_sum2")]] = np.asarray(t.data, dtype=np.float32).reshape(-1)
-        elif t.name.endswith(".counts"):
-            counts[t.name[: -len(".counts")]] = np.asarray(t.data, dtype=np.float32).reshape(-1)
-    out = {}
-    for name, s in sums.items():
-        c = counts.get(name)
-        if c is None:
+    """Importance weights per tensor from a GGUF imatrix file: for every tensor name with
+    both a `<name>.in_sum2` (summed squared activations per column, one row per expert)
+    and a `<name>.counts` (tokens seen per expert), the per-column mean in_sum2 / count as
+    float32, and 0 for an expert that saw no tokens. Flattened over experts; the caller
+    takes the first k values (the reference's convention, quant-studio.py:454-455)."""
+    parts: dict[str, dict[str, np.ndarray]] = {}
+    for t in GGUFReader(path).tensors:
+        base, dot, kind = t.name.rpartition(".")
+        if dot and kind in ("in_sum2", "counts"):
+            parts.setdefault(base, {})[kind] = np.asarray(t.data, dtype=np.float32).ravel()
+    weights = {}
+    for base, p in parts.items():
+        if "in_sum2" not in p or "counts" not in p:
             continue
-        e = s.reshape(c.size, -1)
-        w = np.zeros_like(e)
-        np.divide(e, c[:, None], out=w, where=c[:, None] > 0)
-        out[name] = w.reshape(-1)
-    return out
+        n = p["counts"][:, None]                      # (experts, 1)
+        sums = p["in_sum2"].reshape(n.shape[0], -1)   # (experts, columns)
+        seen = n > 0
+        weights[base] = np.where(seen, sums / np.where(seen, n, np.float32(1)), np.float32(0)).ravel()
+    return weights
 
 
 def fmt_size(n: float) -> str:
