@@ -58,12 +58,17 @@ ALG_OPS = {("q4_k", True): 655, ("q4_k", False): 21 * 17 + 11 + 3 + 4 + 7,
            # 93.3 / 13.3 / 50.8 / 38.9
            ("iq2_xxs", True): round(39.1 * 33) + 14 * 12 + 15 + 110, ("iq2_xs", True): round(93.3 * 33) + 20 * 12 + 15,
            ("iq2_s", True): round(13.3 * 33) + 20 * 12 + 15, ("iq3_xxs", True): round(50.8 * 17) + 32 * 12 + 15,
-           ("iq3_s", True): round(38.9 * 17) + 20 * 12 + 15}
+           ("iq3_s", True): round(38.9 * 17) + 20 * 12 + 15,
+           # the 32-value block formats: block max/min, one scale, 3-4 ops per value
+           ("q4_1", False): 10, ("q5_0", False): 10, ("q5_1", False): 10, ("q8_0", False): 8}
 ALG_BYTES_OUT = {"q4_0": 18 / 32, "q2_k": 84 / 256, "q3_k": 110 / 256, "q4_k": 144 / 256,
                  "q5_k": 176 / 256, "q6_k": 210 / 256, "iq4_xs": 136 / 256, "iq2_xxs": 66 / 256,
-                 "iq2_xs": 74 / 256, "iq2_s": 82 / 256, "iq3_xxs": 98 / 256, "iq3_s": 110 / 256}
-TYPE_IDS = {"q4_0": 2, "q2_k": 10, "q3_k": 11, "q4_k": 12, "q5_k": 13, "q6_k": 14, "iq2_xxs": 16,
-            "iq2_xs": 17, "iq3_xxs": 18, "iq3_s": 21, "iq2_s": 22, "iq4_xs": 23}
+                 "iq2_xs": 74 / 256, "iq2_s": 82 / 256, "iq3_xxs": 98 / 256, "iq3_s": 110 / 256,
+                 "q4_1": 20 / 32, "q5_0": 22 / 32, "q5_1": 24 / 32, "q8_0": 34 / 32}
+TYPE_IDS = {"q4_0": 2, "q4_1": 3, "q5_0": 6, "q5_1": 7, "q8_0": 8, "q2_k": 10, "q3_k": 11, "q4_k": 12,
+            "q5_k": 13, "q6_k": 14, "iq2_xxs": 16, "iq2_xs": 17, "iq3_xxs": 18, "iq3_s": 21, "iq2_s": 22,
+            "iq4_xs": 23}
+IMATRIX_FREE = ("q4_0", "q4_1", "q5_0", "q5_1", "q8_0")  # formats that ignore importance weights
 
 
 def measured_peaks() -> dict:
@@ -208,11 +213,15 @@ def main() -> None:
     ap.add_argument("--scheme", default=None, help="--op cli: scheme (default Q4_K_M for 4b, IQ3_XXS for 8b)")
     ap.add_argument("--model-dir", default=None, help="--op cli: directory for the synthetic model and output")
     ap.add_argument("--mem", default="4G", help="--op cli: the CLI's --mem")
+    ap.add_argument("--no-configs", dest="configs", action="store_false",
+                    help="skip the config-1 / config-3 keys of the default line")
     args = ap.parse_args()
     if args.op == "cli":
         bench_cli(args)
         return
     args.warmup = max(args.warmup, 3)
+    if args.qtype in IMATRIX_FREE:
+        args.imatrix = False
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -298,6 +307,7 @@ def main() -> None:
     sm_mhz = (clocks or {}).get("sm_mhz") or peaks.get("clocks_under_load", {}).get("sm_mhz_median") or 1965.0
     ops = ALG_OPS.get((args.qtype, args.imatrix))
     elems_per_launch = n_elem / len(xs)
+    peak_info = {"sm_count": sm_count, "sm_mhz": sm_mhz, "peaks": peaks}
     alg_bytes = elems_per_launch * (2 + ALG_BYTES_OUT[args.qtype])
     hbm = {"bound": "hbm", "achieved": round(alg_bytes / (launch_ms * 1e-3) / 1e9, 2), "peak": peaks["hbm_gbs"],
            "unit": "GB/s", "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"}
@@ -337,6 +347,12 @@ def main() -> None:
             "kernel_ms_by_shape": {f"{r}x{c}": round(statistics.median(k[i] for k in kern_ms), 4)
                                    for i, (r, c) in enumerate(SHAPES_C2) if i in (0, len(SHAPES_C2) - 1)},
             "e2e": e2e}
+    if world == 1 and args.op == "quantize" and args.qtype == "q4_k" and args.configs:
+        # the north star's other single-GPU configs, on the same device, after the headline
+        del xs, outs
+        torch.cuda.empty_cache()
+        line["config1"] = bench_config1(torch, _native, device, args, peak_info)
+        line["config3"] = bench_config3(torch, _native, device, args, peak_info)
     if rank == 0 and world == 1 and args.cpu_baseline:
         def gpu_quantize(a, qw):
             xd = torch.from_numpy(a).to(device).to(torch.bfloat16)  # a holds bf16-representable values
@@ -348,6 +364,126 @@ def main() -> None:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def graph_of(torch, stream, fn):
+    """fn() captured into a CUDA graph on `stream` (after one eager run), so that a batch of
+    short launches is timed without the host's per-call overhead between them."""
+    with torch.cuda.stream(stream):
+        fn()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+        fn()
+    return g
+
+
+def bench_config1(torch, _native, device, args, info) -> dict:
+    """Q4_0 (no imatrix) of one bf16 4096 x 4096 tensor, N(0, 0.02) with
+    0.1 % N(0, 0.5) outliers. One launch moves 43 MB, which fits the 126 MB L2, so the launches
+    rotate over R copies of the tensor (R x 43 MB > 3 x L2): a copy is evicted by the time it is
+    quantized again. Time = a CUDA graph of R launches, replayed, divided by R (launch gaps
+    included)."""
+    rows = cols = 4096
+    R = 9
+    xs, _ = make_inputs(torch, device, seed=7, shapes=[(rows, cols)])
+    x0 = xs[0]
+    copies = [x0] + [x0.clone() for _ in range(R - 1)]
+    rb = _native.row_bytes(2, cols)
+    outs = [torch.empty((rows, rb), dtype=torch.uint8, device=device) for _ in range(R)]
+    stream = torch.cuda.Stream(device)
+
+    def batch():
+        for x, o in zip(copies, outs):
+            _native.quantize_into(2, x, None, o, stream)
+
+    g = graph_of(torch, stream, batch)
+    reps = max(args.steps, 10)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):  # replay() launches on the current stream
+        for _ in range(args.warmup):
+            g.replay()
+        stream.synchronize()
+        with ClockSampler(device.index) as clk:
+            torch.cuda.synchronize()
+            t0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            t1.record(stream)
+            stream.synchronize()
+    us = t0.elapsed_time(t1) * 1e3 / (reps * R)
+    alg = rows * cols * (2 + 18 / 32)
+    peaks = info["peaks"]
+    ach = alg / (us * 1e-6) / 1e9
+    ok = all(torch.equal(o, outs[0]) for o in outs[1:])
+    del g
+    return {"workload": "BASELINE configs[0]: Q4_0, no imatrix, one 4096x4096 bf16 tensor (43.0 MB per launch); "
+                        f"launches rotate over {R} copies (L2 cold for every launch)",
+            "metric": "input GB/s quantized (bf16->q4_0)", "value": round(2 * rows * cols / (us * 1e-6) / 1e9, 2),
+            "unit": "GB/s", "us_per_launch": round(us, 3), "launches": reps * R,
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(ach / peaks["hbm_gbs"], 4), "bytes_per_value": 2 + 18 / 32,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
+            "copies_identical": ok, "clocks": clk.summary()}
+
+
+def bench_config3(torch, _native, device, args, info) -> dict:
+    """IQ2_XXS with imatrix over the configs[1] tensor set, plus the
+    151936 x 2560 token embedding as Q4_0 (--token-embedding-type q4_0). One step = the nine
+    launches; inputs (1.38 GB) are larger than L2."""
+    shapes = SHAPES_C2 + [(151936, 2560)]
+    xs, qws = make_inputs(torch, device, seed=3, shapes=shapes)
+    types = [16] * len(SHAPES_C2) + [2]
+    qws[-1] = None
+    outs = [torch.empty((x.shape[0], _native.row_bytes(t, x.shape[1])), dtype=torch.uint8, device=device)
+            for x, t in zip(xs, types)]
+    stream = torch.cuda.Stream(device)
+    steps = max(3, min(args.steps, 10))
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in xs]
+          for _ in range(steps)]
+
+    def step(e=None):
+        for i, (x, q, o, t) in enumerate(zip(xs, qws, outs, types)):
+            if e is not None:
+                e[i][0].record(stream)
+            _native.quantize_into(t, x, q, o, stream)
+            if e is not None:
+                e[i][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    stream.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clk:
+        torch.cuda.synchronize()
+        t0.record(stream)
+        for s in range(steps):
+            step(ev[s])
+        t1.record(stream)
+        stream.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    n_iq = sum(r * c for r, c in SHAPES_C2)
+    n_emb = 151936 * 2560
+    iq_ms = statistics.median(sum(a.elapsed_time(b) for a, b in e[:-1]) for e in ev)
+    emb_ms = statistics.median(e[-1][0].elapsed_time(e[-1][1]) for e in ev)
+    lane_peak = info["sm_count"] * 128 * info["sm_mhz"] * 1e6 / 1e12
+    ops = ALG_OPS[("iq2_xxs", True)]
+    iq_ach = ops * n_iq / (iq_ms * 1e-3) / 1e12
+    emb_ach = n_emb * (2 + 18 / 32) / (emb_ms * 1e-3) / 1e9
+    peaks = info["peaks"]
+    del xs, outs
+    return {"workload": "BASELINE configs[2]: IQ2_XXS + imatrix over 4 x 4096x4096 + 4 x 14336x4096 bf16, "
+                        "plus a 151936x2560 bf16 token embedding to Q4_0",
+            "metric": "input GB/s quantized (bf16->iq2_xxs mix)", "value": round(2 * (n_iq + n_emb) / (ms * 1e-3) / 1e9, 3),
+            "unit": "GB/s", "ms_per_step": round(ms, 3), "steps": steps,
+            "iq2_xxs": {"ms_per_step": round(iq_ms, 3), "value": round(2 * n_iq / (iq_ms * 1e-3) / 1e9, 3),
+                        "roofline": {"bound": "fp32-lane", "achieved": round(iq_ach, 3), "peak": round(lane_peak, 3),
+                                     "unit": "Tops/s", "ops_per_value": ops, "frac": round(iq_ach / lane_peak, 4)}},
+            "q4_0_embedding": {"ms": round(emb_ms, 4), "roofline": {"bound": "hbm", "achieved": round(emb_ach, 1),
+                                                                    "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                                                    "frac": round(emb_ach / peaks["hbm_gbs"], 4)}},
+            "clocks": clk.summary()}
 
 
 def bench_decode_op(torch, _native, gt, xs, qws, outs, stream, device, args, config, n_elem):
@@ -487,7 +623,7 @@ def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, wor
     h2d_done, kern_done, d2h_done = ([torch.cuda.Event() for _ in range(nbuf)] for _ in range(3))
     launches = [0]
 
-    def one_step():
+    def one_step(kernels=True):
         slot = 0
         for x_h, q, o_h in zip(h_in, qws, h_out):
             n, k = x_h.shape
@@ -502,8 +638,9 @@ def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, wor
                 h2d_done[slot].record(s_h2d)
                 s_comp.wait_event(h2d_done[slot])
                 s_comp.wait_event(d2h_done[slot])       # the slot's previous blocks are on the host
-                _native.quantize_into(gt, din, q, dout, s_comp)
-                launches[0] += 1
+                if kernels:
+                    _native.quantize_into(gt, din, q, dout, s_comp)
+                    launches[0] += 1
                 kern_done[slot].record(s_comp)
                 s_d2h.wait_event(kern_done[slot])
                 with torch.cuda.stream(s_d2h):
@@ -527,11 +664,30 @@ def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, wor
     torch.cuda.synchronize()
     ms = allmax(t0.elapsed_time(t1)) / args.steps
     ok = all(torch.equal(o_h.to(device), o) for o_h, o in zip(h_out, outs))
-    return {"value": round(world * 2 * n_elem / (ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+    # the same copies with the kernels left out, on every rank at once: the host<->device
+    # ceiling of this pipeline on this box (PCIe and host memory shared by all ranks)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(s_h2d)
+    for _ in range(args.steps):
+        one_step(kernels=False)
+    s_h2d.wait_stream(s_comp)
+    s_h2d.wait_stream(s_d2h)
+    c1.record(s_h2d)
+    torch.cuda.synchronize()
+    ms_copy = allmax(c0.elapsed_time(c1)) / args.steps
+    value = world * 2 * n_elem / (ms * 1e-3) / 1e9
+    ceiling = world * 2 * n_elem / (ms_copy * 1e-3) / 1e9
+    return {"value": round(value, 3), "unit": "GB/s",
             "h2d_bytes_per_step": int(sum(x.numel() * x.element_size() for x in xs)),
             "d2h_bytes_per_step": int(sum(o.numel() for o in outs)), "ms_per_step": round(ms, 3),
             "gpu_launches": launches[0], "pipeline": f"{chunk_rows}-row chunks, {nbuf} device slots, H2D / kernel / D2H streams",
-            "matches_device_resident_output": ok}
+            "matches_device_resident_output": ok,
+            "copy_ceiling": {"value": round(ceiling, 3), "unit": "GB/s", "ms_per_step": round(ms_copy, 3),
+                             "what": "the same H2D / D2H copies and chunking with no kernels, all ranks at once"},
+            "frac_of_copy_ceiling": round(value / ceiling, 4)}
 
 
 def cpu_baseline(args, gpu_quantize=None) -> dict:

@@ -38,6 +38,10 @@ extern "C" {
 
 /* GGML type ids this library quantizes to (gguf GGMLQuantizationType). */
 #define QS_TYPE_Q4_0 2
+#define QS_TYPE_Q4_1 3   /* Q4_1 / Q5_0 / Q5_1 / Q8_0: no kernel in the reference (see qs_quantize) */
+#define QS_TYPE_Q5_0 6
+#define QS_TYPE_Q5_1 7
+#define QS_TYPE_Q8_0 8
 #define QS_TYPE_Q2_K 10
 #define QS_TYPE_Q3_K 11
 #define QS_TYPE_Q4_K 12
@@ -90,6 +94,11 @@ int qs_row_bytes(int ggml_type, int64_t k, int64_t* out_bytes);
  *   dst_row_bytes  >= qs_row_bytes(type, k)
  *   stream         cudaStream_t (NULL = legacy default stream)
  * Output bytes are identical to the reference's eager CPU path for the same values.
+ * Q4_1, Q5_0, Q5_1 and Q8_0 have no kernel in the reference, whose type-mix policy still
+ * selects them (kernels/scheme.py:375 shape fallbacks, :521-523 ffn_down under Q4_0 / Q5_0
+ * with an importance matrix) and whose CLI then stops (quant-studio.py:396-399); here they
+ * give the bytes of gguf-py's quantize_blocks for those types (the ggml-quants.c reference
+ * rows) and, like the reference's Q4_0, ignore qw.
  */
 int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_rows, int64_t k,
                 const float* qw, void* dst, int64_t dst_row_bytes, void* stream);
@@ -158,6 +167,14 @@ int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row_bytes,
  */
 int qs_tensor_error_noalloc(int ggml_type, const void* blocks, int64_t blocks_row_bytes, const void* x,
                             int x_type, int64_t n_rows, int64_t k, const float* qw, double* out, void* stream);
+
+/*
+ * Fault word of `device`: bit 0 is set when a quantize kernel gave up waiting for one of its
+ * own bulk copies (every wait in the kernels is bounded; on that path the kernel records
+ * the fault and returns instead of hanging the GPU). Synchronous; clears the word.
+ * No counterpart in the reference (its kernels have no waits).
+ */
+int qs_device_fault(int device, int* bits);
 
 /* Message of the calling thread's last failure ("" if none). */
 const char* qs_last_error(void);

@@ -13,7 +13,9 @@
  *   - torch.round is round-half-even (nearbyintf);
  *   - `.sum(-1)` on a float32 CPU tensor follows torch's 8-lane cascade (tsum*),
  *     the reference's own seq_sum / tree_sum keep their explicit orders.
- * Pinned against the fixtures in tests/golden (outputs of the reference itself).
+ * Pinned against the fixtures in tests/golden (outputs of the reference itself); the four
+ * formats the reference has no kernel for (Q4_1, Q5_0, Q5_1, Q8_0) restate gguf-py's
+ * quantizers and are pinned against gguf-py on the same inputs (tests/test_oracle_golden.py).
  */
 #include <math.h>
 #include <pthread.h>
@@ -335,6 +337,87 @@ static void q4_0_block(const f32 *x, uint8_t *out) {
     uint8_t q[32];
     for (int i = 0; i < 32; i++) q[i] = (uint8_t)clampf(floorf(x[i] * id + 8.5f), 0.0f, 15.0f);
     for (int i = 0; i < 16; i++) out[2 + i] = (uint8_t)(q[i] + q[16 + i] * 16);
+}
+
+/* ------------------------------------------------------------------ */
+/* Q4_1 / Q5_0 / Q5_1 / Q8_0: no kernel in the reference; restated from  */
+/* gguf-py 0.19.0 gguf/quants.py (Q4_1 :254-289, Q5_0 :291-331, Q5_1     */
+/* :333-376, Q8_0 :378-395, np_roundf :43-47), the float32 numpy code of */
+/* ggml-quants.c's quantize_row_*_ref. numpy casts float -> uint8/int8   */
+/* through a 32-bit integer: non-finite or out-of-range values give 0.   */
+/* ------------------------------------------------------------------ */
+static inline int32_t np_i32(f32 v) {
+    if (!isfinite(v) || v >= 2147483648.0f || v < -2147483648.0f) return 0;
+    return (int32_t)v;
+}
+static inline f32 np_roundf1(f32 v) {
+    f32 a = fabsf(v), f = floorf(a);
+    f32 b = f + floorf(2.0f * (a - f));
+    return v > 0.0f ? b : (v < 0.0f ? -b : (v == 0.0f ? 0.0f * b : v));
+}
+static inline f32 inv_or_zero(f32 d) { return d == 0.0f ? 0.0f : 1.0f / d; }
+
+/* levels q[32] -> qs[16] nibble pairs (value j low, value j + 16 high) */
+static void pack_nibbles(const int *q, uint8_t *qs) {
+    for (int j = 0; j < 16; j++) qs[j] = (uint8_t)((q[j] & 0x0F) | ((q[16 + j] & 0x0F) << 4));
+}
+static void pack_high_bits(const int *q, uint8_t *qh) {
+    for (int m = 0; m < 4; m++) {
+        int v = 0;
+        for (int j = 0; j < 8; j++) v |= ((q[8 * m + j] >> 4) != 0) << j;
+        qh[m] = (uint8_t)v;
+    }
+}
+
+static void q4_1_block(const f32 *x, uint8_t *out) {
+    f32 mx = x[0], mn = x[0];
+    for (int i = 1; i < 32; i++) { mx = x[i] > mx ? x[i] : mx; mn = x[i] < mn ? x[i] : mn; }
+    f32 d = (mx - mn) / 15.0f, id = inv_or_zero(d);
+    int q[32];
+    for (int i = 0; i < 32; i++) {
+        int v = np_i32(truncf((x[i] - mn) * id + 0.5f)) & 0xFF;
+        q[i] = v > 15 ? 15 : v;
+    }
+    put16(out, f16_bits(d));
+    put16(out + 2, f16_bits(mn));
+    pack_nibbles(q, out + 4);
+}
+
+static void q5_0_block(const f32 *x, uint8_t *out) {
+    f32 amax, mx;
+    absmax_first(x, 32, &amax, &mx);
+    f32 d = mx / -16.0f, id = inv_or_zero(d);
+    int q[32];
+    for (int i = 0; i < 32; i++) {
+        int v = np_i32(truncf(x[i] * id + 16.5f)) & 0xFF;
+        q[i] = v > 31 ? 31 : v;
+    }
+    put16(out, f16_bits(d));
+    pack_high_bits(q, out + 2);
+    pack_nibbles(q, out + 6);
+}
+
+static void q5_1_block(const f32 *x, uint8_t *out) {
+    f32 mx = x[0], mn = x[0];
+    for (int i = 1; i < 32; i++) { mx = x[i] > mx ? x[i] : mx; mn = x[i] < mn ? x[i] : mn; }
+    f32 d = (mx - mn) / 31.0f, id = inv_or_zero(d);
+    int q[32];
+    for (int i = 0; i < 32; i++) {
+        int v = np_i32(truncf((x[i] - mn) * id + 0.5f)) & 0xFF;
+        q[i] = v > 31 ? 31 : v;
+    }
+    put16(out, f16_bits(d));
+    put16(out + 2, f16_bits(mn));
+    pack_high_bits(q, out + 4);
+    pack_nibbles(q, out + 8);
+}
+
+static void q8_0_block(const f32 *x, uint8_t *out) {
+    f32 amax = fabsf(x[0]);
+    for (int i = 1; i < 32; i++) amax = fabsf(x[i]) > amax ? fabsf(x[i]) : amax;
+    f32 d = amax / 127.0f, id = inv_or_zero(d);
+    put16(out, f16_bits(d));
+    for (int i = 0; i < 32; i++) out[2 + i] = (uint8_t)(np_i32(np_roundf1(x[i] * id)) & 0xFF);
 }
 
 /* ------------------------------------------------------------------ */
@@ -1179,6 +1262,10 @@ static int type_info(int type, int *qk, int *bytes, sb_fn *fn, int *needs_qw) {
     *needs_qw = 0;
     switch (type) {
     case OQ_Q4_0: *qk = 32; *bytes = 18; *fn = NULL; return 0;
+    case OQ_Q4_1: *qk = 32; *bytes = 20; *fn = NULL; return 0;
+    case OQ_Q5_0: *qk = 32; *bytes = 22; *fn = NULL; return 0;
+    case OQ_Q5_1: *qk = 32; *bytes = 24; *fn = NULL; return 0;
+    case OQ_Q8_0: *qk = 32; *bytes = 34; *fn = NULL; return 0;
     case OQ_Q2_K: *qk = QK_K; *bytes = 84; *fn = q2_k_sb; return 0;
     case OQ_Q3_K: *qk = QK_K; *bytes = 110; *fn = q3_k_sb; return 0;
     case OQ_Q4_K: *qk = QK_K; *bytes = 144; *fn = NULL; return 0;
@@ -1215,6 +1302,10 @@ static void run_block(const job_t *j, int64_t b) {
     const f32 *qb = j->qw ? j->qw + (b % j->nb_row) * j->qk : NULL;
     uint8_t *ob = j->out + b * j->bytes;
     if (j->type == OQ_Q4_0) q4_0_block(xb, ob);
+    else if (j->type == OQ_Q4_1) q4_1_block(xb, ob);
+    else if (j->type == OQ_Q5_0) q5_0_block(xb, ob);
+    else if (j->type == OQ_Q5_1) q5_1_block(xb, ob);
+    else if (j->type == OQ_Q8_0) q8_0_block(xb, ob);
     else if (j->type == OQ_Q4_K) q45_k_sb(xb, qb, 15, ob);
     else if (j->type == OQ_Q5_K) q45_k_sb(xb, qb, 31, ob);
     else j->fn(xb, qb, ob);

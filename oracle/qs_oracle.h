@@ -8,7 +8,7 @@ extern "C" {
 
 /* GGML type ids (gguf GGMLQuantizationType) */
 enum {
-    OQ_Q4_0 = 2, OQ_Q2_K = 10, OQ_Q3_K = 11, OQ_Q4_K = 12, OQ_Q5_K = 13, OQ_Q6_K = 14,
+    OQ_Q4_0 = 2, OQ_Q4_1 = 3, OQ_Q5_0 = 6, OQ_Q5_1 = 7, OQ_Q8_0 = 8, OQ_Q2_K = 10, OQ_Q3_K = 11, OQ_Q4_K = 12, OQ_Q5_K = 13, OQ_Q6_K = 14,
     OQ_IQ2_XXS = 16, OQ_IQ2_XS = 17, OQ_IQ3_XXS = 18, OQ_IQ3_S = 21, OQ_IQ2_S = 22, OQ_IQ4_XS = 23,
 };
 

@@ -33,6 +33,8 @@ const TypeInfo kTypes[] = {
     {qs::QS_Q4_K, 256, 144, 0},    {qs::QS_Q5_K, 256, 176, 0},     {qs::QS_Q6_K, 256, 210, 0},
     {qs::QS_IQ2_XXS, 256, 66, 1},  {qs::QS_IQ2_XS, 256, 74, 1},    {qs::QS_IQ3_XXS, 256, 98, 0},
     {qs::QS_IQ3_S, 256, 110, 0},   {qs::QS_IQ2_S, 256, 82, 1},     {qs::QS_IQ4_XS, 256, 136, 0},
+    {qs::QS_Q4_1, 32, 20, 0},      {qs::QS_Q5_0, 32, 22, 0},       {qs::QS_Q5_1, 32, 24, 0},
+    {qs::QS_Q8_0, 32, 34, 0},
 };
 
 const TypeInfo* find_type(int t) {
@@ -278,7 +280,9 @@ QS_API int qs_quantize(int ggml_type, const void* src, int src_type, int64_t n_r
     qs::LaunchCtx ctx{static_cast<cudaStream_t>(stream), device, d->num_sms};
     if (is_iq(ggml_type) && (e = qs::iq_tables_ensure(d->iq, ggml_type)) != cudaSuccess)
         return cuda_fail(e, "building lattice tables");
-    e = is_iq(ggml_type) ? qs::launch_iq(ggml_type, a, ctx, d->iq) : qs::launch_kquant(ggml_type, a, ctx);
+    e = is_iq(ggml_type)             ? qs::launch_iq(ggml_type, a, ctx, d->iq)
+        : qs::is_blk32(ggml_type)    ? qs::launch_blk32(ggml_type, a, ctx)
+                                     : qs::launch_kquant(ggml_type, a, ctx);
     if (e != cudaSuccess) return cuda_fail(e, "kernel launch");
     return QS_OK;
 }
@@ -360,6 +364,17 @@ QS_API int qs_tensor_error(int ggml_type, const void* blocks, int64_t blocks_row
     cudaError_t ef = cudaFreeAsync(partial, st);
     if (e != cudaSuccess) return cuda_fail(e, "tensor error launch");
     return ef == cudaSuccess ? QS_OK : cuda_fail(ef, "cudaFreeAsync (partial sums)");
+}
+
+QS_API int qs_device_fault(int device, int* bits) {
+    if (!bits) return fail(QS_EINVAL, "null bits");
+    CurrentContextGuard keep;
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    unsigned int b = 0;
+    if ((e = qs::read_fault_bits(&b, true)) != cudaSuccess) return cuda_fail(e, "reading the fault word");
+    *bits = (int)b;
+    return QS_OK;
 }
 
 static_assert(qs::NA_MAX_PARTIALS == QS_NOALLOC_MAX_PARTIALS, "static scratch size and its public constant differ");

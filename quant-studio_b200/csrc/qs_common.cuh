@@ -188,7 +188,10 @@ __device__ __forceinline__ void store_bytes(uint8_t* __restrict__ dst, const uin
     int body = (nbytes - head) / 16;
     uint4* d4 = reinterpret_cast<uint4*>(dst + head);
     const uint8_t* s = src + head;
-    if (((uintptr_t)s & 3) == 0) {
+    if (((uintptr_t)s & 15) == 0) {
+        const uint4* s16 = reinterpret_cast<const uint4*>(s);
+        for (int i = tid; i < body; i += nthreads) d4[i] = s16[i];
+    } else if (((uintptr_t)s & 3) == 0) {
         for (int i = tid; i < body; i += nthreads) {
             const uint32_t* s4 = reinterpret_cast<const uint32_t*>(s + 16 * i);
             d4[i] = make_uint4(s4[0], s4[1], s4[2], s4[3]);

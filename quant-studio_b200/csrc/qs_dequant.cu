@@ -1,7 +1,7 @@
 // Block decode (GGUF dequantization) and the decode-error checkers (sm_100a).
 //
 // The decode of every block format restates gguf-py's numpy dequantizers
-// (gguf/quants.py, gguf 0.19.0: Q4_0 / Q2_K / Q3_K / Q4_K / Q5_K / Q6_K / IQ2_XXS /
+// (gguf/quants.py, gguf 0.19.0: Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 / Q2_K / Q3_K / Q4_K / Q5_K / Q6_K / IQ2_XXS /
 // IQ2_XS / IQ2_S / IQ3_XXS / IQ3_S / IQ4_XS .dequantize_blocks), which is what the
 // reference's correctness harness decodes with (tools/dev_harness.py:108-109): the same
 // float32 operations in the same order, so the values are bit-identical. The checkers
@@ -55,6 +55,58 @@ template <> struct Dq<QS_Q4_0> {
             const int q = p < 16 ? (b[2 + p + i] & 0xF) : (b[2 + p - 16 + i] >> 4);
             v[i] = d * (float)(q - 8);
         }
+    }
+};
+
+// Q4_1 (gguf Q4_1.dequantize_blocks): (d * q) + m, q as in Q4_0 without the offset
+template <> struct Dq<QS_Q4_1> {
+    static constexpr int QK = 32, BB = 20;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b), m = f16_at(b + 2);
+        const int p = 8 * t;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int q = p < 16 ? (b[4 + p + i] & 0xF) : (b[4 + p - 16 + i] >> 4);
+            v[i] = d * (float)q + m;
+        }
+    }
+};
+
+// Q5_0 (gguf Q5_0.dequantize_blocks): d * ((ql | qh << 4) - 16), bit j of qh for value j
+template <> struct Dq<QS_Q5_0> {
+    static constexpr int QK = 32, BB = 22;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b);
+        const int p = 8 * t;
+        const uint32_t hb = b[2 + t];  // qh bits of values p .. p + 7
+        const uint8_t* ql = b + 6 + (p & 15);
+        const int sh = p < 16 ? 0 : 4;
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = d * (float)((((ql[i] >> sh) & 0xF) | (int)(((hb >> i) & 1u) << 4)) - 16);
+    }
+};
+
+// Q5_1 (gguf Q5_1.dequantize_blocks): (d * (ql | qh << 4)) + m
+template <> struct Dq<QS_Q5_1> {
+    static constexpr int QK = 32, BB = 24;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b), m = f16_at(b + 2);
+        const int p = 8 * t;
+        const uint32_t hb = b[4 + t];  // qh bits of values p .. p + 7
+        const uint8_t* ql = b + 8 + (p & 15);
+        const int sh = p < 16 ? 0 : 4;
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = d * (float)(((ql[i] >> sh) & 0xF) | (int)(((hb >> i) & 1u) << 4)) + m;
+    }
+};
+
+// Q8_0 (gguf Q8_0.dequantize_blocks): x * d with x the int8 values
+template <> struct Dq<QS_Q8_0> {
+    static constexpr int QK = 32, BB = 34;
+    __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
+        const float d = f16_at(b);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = (float)(int8_t)b[2 + 8 * t + i] * d;
     }
 };
 
@@ -414,6 +466,10 @@ template <int MODE>
 cudaError_t launch_dq_mode(int type, const DqArgs& a, const LaunchCtx& ctx, int grid) {
     switch (type) {
     case QS_Q4_0: return launch_dq_t<QS_Q4_0, MODE>(a, ctx, grid);
+    case QS_Q4_1: return launch_dq_t<QS_Q4_1, MODE>(a, ctx, grid);
+    case QS_Q5_0: return launch_dq_t<QS_Q5_0, MODE>(a, ctx, grid);
+    case QS_Q5_1: return launch_dq_t<QS_Q5_1, MODE>(a, ctx, grid);
+    case QS_Q8_0: return launch_dq_t<QS_Q8_0, MODE>(a, ctx, grid);
     case QS_Q2_K: return launch_dq_t<QS_Q2_K, MODE>(a, ctx, grid);
     case QS_Q3_K: return launch_dq_t<QS_Q3_K, MODE>(a, ctx, grid);
     case QS_Q4_K: return launch_dq_t<QS_Q4_K, MODE>(a, ctx, grid);
@@ -429,7 +485,9 @@ cudaError_t launch_dq_mode(int type, const DqArgs& a, const LaunchCtx& ctx, int 
     }
 }
 
-int block_qk(int type) { return type == QS_Q4_0 ? 32 : 256; }
+int block_qk(int type) {
+    return type == QS_Q4_0 || type == QS_Q4_1 || type == QS_Q5_0 || type == QS_Q5_1 || type == QS_Q8_0 ? 32 : 256;
+}
 
 DqArgs make_args(int type, const DqCall& c, const IqTables* t) {
     DqArgs a;

@@ -11,7 +11,7 @@ namespace qs {
 
 // GGML type ids (gguf GGMLQuantizationType)
 enum QsType : int {
-    QS_Q4_0 = 2, QS_Q2_K = 10, QS_Q3_K = 11, QS_Q4_K = 12, QS_Q5_K = 13, QS_Q6_K = 14,
+    QS_Q4_0 = 2, QS_Q4_1 = 3, QS_Q5_0 = 6, QS_Q5_1 = 7, QS_Q8_0 = 8, QS_Q2_K = 10, QS_Q3_K = 11, QS_Q4_K = 12, QS_Q5_K = 13, QS_Q6_K = 14,
     QS_IQ2_XXS = 16, QS_IQ2_XS = 17, QS_IQ3_XXS = 18, QS_IQ3_S = 21, QS_IQ2_S = 22, QS_IQ4_XS = 23,
 };
 
@@ -33,6 +33,12 @@ struct LaunchCtx {
 struct IqTables;  // per-device lattice tables (qs_iq.cu)
 
 cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx);
+// 32-value block formats (qs_blk32.cu): Q4_0, Q4_1, Q5_0, Q5_1, Q8_0
+bool is_blk32(int type);
+cudaError_t launch_blk32(int type, const QuantArgs& a, const LaunchCtx& ctx);
+// Fault word of the current device: bit 0 = a kernel gave up waiting for a bulk copy.
+// Synchronous; clears the word when `clear` and it is non-zero.
+cudaError_t read_fault_bits(unsigned int* bits, bool clear);
 cudaError_t launch_iq(int type, const QuantArgs& a, const LaunchCtx& ctx, const IqTables* t);
 cudaError_t iq_tables_create(IqTables** out);  // uploads the codebooks to the current device
 cudaError_t iq_tables_ensure(IqTables* t, int type);  // neighbour tables of type's grid, once

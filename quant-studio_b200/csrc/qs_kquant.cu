@@ -1,4 +1,4 @@
-// K-quant (Q2_K..Q6_K), IQ4_XS and Q4_0 kernels for sm_100a.
+// K-quant (Q2_K..Q6_K) and IQ4_XS kernels for sm_100a.
 //
 // Layout: one thread per quantization group (16 or 32 values in registers), the
 // threads of a superblock are consecutive lanes of one warp, a CTA of 128 or 256 threads
@@ -9,165 +9,6 @@
 #include "qs_kernels.h"
 
 namespace qs {
-
-// ---------------------------------------------------------------------------
-// Q4_0 (kernels/q4_0.py:14-33), HBM-bound. A warp owns tiles of 32 consecutive
-// 32-blocks. Tiles stream into a per-warp ring of shared-memory stages with cp.async
-// (coalesced 16-byte copies, lane l: bytes 16 l + 512 j of the tile), STAGES - 1 tiles
-// ahead of the one being quantized, so memory stays busy without holding the data in
-// registers. Each lane then quantizes one whole block: no shuffles, one reciprocal per
-// block. d = max / -8 is computed as max * -0.125 (the same IEEE value).
-// In the ring, 16-byte chunk i of block b sits at slot CPB * b + (i ^ swz(b)) (CPB = 4 or
-// 8 chunks per block): the 8 lanes of a quarter warp then read 8 distinct 16-byte bank
-// groups when each loads chunk i of its own block.
-// ---------------------------------------------------------------------------
-template <int CPB>
-__device__ __forceinline__ int q40_slot(int b, int i) {
-    return CPB * b + (i ^ (CPB == 4 ? ((b >> 1) & 3) : (b & 7)));
-}
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
-template <int ES>  // source element size in bytes
-__global__ void __launch_bounds__(256, 3) q4_0_kernel(QuantArgs a) {
-    constexpr int BB = 18, WARPS = 8, TILE = 32 * 32 * ES, NV = TILE / 512, STAGES = ES == 2 ? 4 : 3;
-    extern __shared__ __align__(16) uint8_t q40_smem[];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint8_t* ring = q40_smem + warp * (STAGES * TILE + 32 * BB);
-    uint8_t* so = ring + STAGES * TILE;
-    const uint8_t* src = static_cast<const uint8_t*>(a.src);
-    const int64_t ntile = (a.nblk + 31) / 32, lim = a.nblk * 32 * ES;
-    const int64_t stride = (int64_t)gridDim.x * WARPS;
-    const int64_t t_first = (int64_t)blockIdx.x * WARPS + warp;
-    constexpr int CPB = 2 * ES;  // 16-byte chunks per 32-value block
-    auto issue = [&](int64_t t, int stage) {  // one commit group per tile, empty past the end
-        if (t < ntile) {
-#pragma unroll
-            for (int j = 0; j < NV; j++) {
-                const int64_t off = t * TILE + 512 * j + 16 * lane;
-                const int g = 32 * j + lane;  // chunk of the tile
-                cp_async16(ring + stage * TILE + 16 * q40_slot<CPB>(g / CPB, g % CPB), off < lim ? src + off : src,
-                           off < lim ? 16 : 0);
-            }
-        }
-        cp_async_commit();
-    };
-#pragma unroll
-    for (int st = 0; st < STAGES - 1; st++) issue(t_first + st * stride, st);
-    int stage = 0;
-    for (int64_t tile = t_first; tile < ntile; tile += stride) {
-        issue(tile + (STAGES - 1) * stride, (stage + STAGES - 1) % STAGES);
-        cp_async_wait<STAGES - 1>();  // this lane's copies of `tile` have landed
-        __syncwarp();                 // ... and every other lane's
-        const int nvalid = (int)min((int64_t)32, a.nblk - tile * 32);
-        float x[32], mx, mn;
-        const uint4* blk = reinterpret_cast<const uint4*>(ring + stage * TILE);
-        if (ES == 4) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float4 f = reinterpret_cast<const float4*>(blk)[q40_slot<CPB>(lane, i)];
-                x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
-            }
-            mx = x[0];
-            mn = x[0];
-#pragma unroll
-            for (int i = 1; i < 32; i++) { mx = fmaxf(mx, x[i]); mn = fminf(mn, x[i]); }
-        } else {
-            // block max / min on packed pairs (exact for 16-bit floats), then widen
-            uint32_t w[16];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint4 t = blk[q40_slot<CPB>(lane, i)];
-                w[4 * i] = t.x; w[4 * i + 1] = t.y; w[4 * i + 2] = t.z; w[4 * i + 3] = t.w;
-            }
-            if (a.src_type == SRC_BF16) {
-                __nv_bfloat162 hx = *reinterpret_cast<const __nv_bfloat162*>(&w[0]), hn = hx;
-#pragma unroll
-                for (int i = 1; i < 16; i++) {
-                    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-                    hx = __hmax2(hx, v);
-                    hn = __hmin2(hn, v);
-                }
-                mx = fmaxf(__low2float(hx), __high2float(hx));
-                mn = fminf(__low2float(hn), __high2float(hn));
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    x[2 * i] = __uint_as_float(w[i] * 65536u);
-                    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-                }
-            } else {
-                __half2 hx = *reinterpret_cast<const __half2*>(&w[0]), hn = hx;
-#pragma unroll
-                for (int i = 1; i < 16; i++) {
-                    const __half2 v = *reinterpret_cast<const __half2*>(&w[i]);
-                    hx = __hmax2(hx, v);
-                    hn = __hmin2(hn, v);
-                }
-                mx = fmaxf(__low2float(hx), __high2float(hx));
-                mn = fminf(__low2float(hn), __high2float(hn));
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    x[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xFFFFu)));
-                    x[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
-                }
-            }
-        }
-        // signed value of the first largest |x|: max and min of the block decide it
-        // unless both +amax and -amax occur, then the first one in order wins
-        float m = mx > -mn ? mx : mn;
-        if (mx == -mn) {
-            float am;
-            absmax_first<32>(x, am, m);
-        }
-        const float d = m * -0.125f;
-        const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
-        // q = clamp(floor(x * id + 8.5), 0, 15). |x * id| <= 8 (plus rounding), so
-        // v = x * id + 8.5 lies in (0, 17): adding 2^23 rounding toward -inf gives the
-        // float 2^23 + floor(v), whose low byte is floor(v) (0..16). Bytes of four values
-        // are gathered with byte permutes and clamped to 15 with one SIMD byte min.
-        uint32_t fb[32];
-#pragma unroll
-        for (int i = 0; i < 32; i++) fb[i] = (uint32_t)__float_as_int(__fadd_rd(x[i] * id + 8.5f, 8388608.0f));
-        uint32_t wq[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const uint32_t lo = __vminu4(__byte_perm(__byte_perm(fb[4 * k], fb[4 * k + 1], 0x0040),
-                                                     __byte_perm(fb[4 * k + 2], fb[4 * k + 3], 0x0040), 0x5410),
-                                         0x0F0F0F0Fu);
-            const uint32_t hi = __vminu4(__byte_perm(__byte_perm(fb[16 + 4 * k], fb[17 + 4 * k], 0x0040),
-                                                     __byte_perm(fb[18 + 4 * k], fb[19 + 4 * k], 0x0040), 0x5410),
-                                         0x0F0F0F0Fu);
-            wq[k] = lo | (hi << 4);
-        }
-        if (lane < nvalid) {
-            uint16_t* o16 = reinterpret_cast<uint16_t*>(so + lane * BB);
-            o16[0] = f16_bits(d);
-#pragma unroll
-            for (int i = 0; i < 4; i++) { o16[1 + 2 * i] = (uint16_t)wq[i]; o16[2 + 2 * i] = (uint16_t)(wq[i] >> 16); }
-        }
-        __syncwarp();
-        if (nvalid == 32 && a.dst_row_bytes == a.row_bytes && (((uintptr_t)a.dst & 15) == 0)) {
-            // whole tile, contiguous rows: 576 bytes = 36 aligned 16-byte chunks
-            uint4* d4 = reinterpret_cast<uint4*>(a.dst + tile * 32 * BB);
-            const uint4* s4 = reinterpret_cast<const uint4*>(so);
-            d4[lane] = s4[lane];
-            if (lane < 4) d4[32 + lane] = s4[32 + lane];
-        } else {
-            store_tile(a, so, tile * 32, nvalid, BB, lane, 32);
-        }
-        __syncwarp();  // the stage and the output staging are free again
-        stage = (stage + 1) % STAGES;
-    }
-    cp_async_wait<0>();
-}
-
-template <int ES>
-constexpr int q4_0_smem() { return 8 * ((ES == 2 ? 4 : 3) * 32 * 32 * ES + 32 * 18); }
 
 // ---------------------------------------------------------------------------
 // Q2_K / Q4_K / Q5_K (kernels/q2_k.py:25-81, q4_k.py:25-79, q5_k.py:25-82)
@@ -668,19 +509,6 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
     const bool imat = a.qw != nullptr;
     cudaStream_t st = ctx.stream;
     switch (type) {
-    case QS_Q4_0: {
-        const int64_t ctas = (a.nblk + 255) / 256;  // 8 warps x tiles of 32 blocks
-        if (a.src_type == SRC_F32) {
-            auto k = q4_0_kernel<4>;
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q4_0_smem<4>());
-            q4_0_kernel<4><<<grid_for(k, ctas, ctx, q4_0_smem<4>()), 256, q4_0_smem<4>(), st>>>(a);
-        } else {
-            auto k = q4_0_kernel<2>;
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, q4_0_smem<2>());
-            q4_0_kernel<2><<<grid_for(k, ctas, ctx, q4_0_smem<2>()), 256, q4_0_smem<2>(), st>>>(a);
-        }
-        break;
-    }
     case QS_Q4_K:
     case QS_Q5_K:
     case QS_Q2_K: {

@@ -22,12 +22,13 @@ MODULES = {
     "q4_0": ("q4_0",), "q2_k": ("q2_k",), "q3_k": ("q3_k",), "q4_k": ("q4_k",), "q5_k": ("q5_k",),
     "q6_k": ("q6_k",), "iq4_xs": ("iq4_xs",), "iq2": ("iq2_xxs",), "iq2_xs": ("iq2_xs",),
     "iq2_s": ("iq2_s",), "iq3_xxs": ("iq3_xxs",), "iq3_s": ("iq3_s",),
+    # formats the reference's policy selects but has no module for
+    "q4_1": ("q4_1",), "q5_0": ("q5_0",), "q5_1": ("q5_1",), "q8_0": ("q8_0",),
 }
 
 QUANT_TYPES: dict[str, QuantSpec] = {}
 for _mod, _names in MODULES.items():
-    _m = types.ModuleType(f"{__name__}.{_mod}", f"{', '.join(n.upper() for n in _names)} through libqsb200 "
-                                               f"(the reference's kernels/{_mod}.py entry point)")
+    _m = types.ModuleType(f"{__name__}.{_mod}", f"{', '.join(n.upper() for n in _names)} through libqsb200")
     _m.SPECS = {}
     for _n in _names:
         setattr(_m, f"quantize_{_n}", _specs.quantizer(_n))

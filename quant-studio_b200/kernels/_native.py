@@ -61,6 +61,8 @@ def lib() -> ctypes.CDLL:
             L.qs_dequantize.argtypes = [ctypes.c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]
             L.qs_block_error.argtypes = [ctypes.c_int, c_vp, c_i64, c_vp, ctypes.c_int, c_i64, c_i64, c_vp, c_vp, c_vp]
             L.qs_tensor_error.argtypes = [ctypes.c_int, c_vp, c_i64, c_vp, ctypes.c_int, c_i64, c_i64, c_vp, c_vp, c_vp]
+            L.qs_tensor_error_noalloc.argtypes = L.qs_tensor_error.argtypes
+            L.qs_device_fault.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
             L.qs_last_error.restype = ctypes.c_char_p
             _lib = L
     return _lib

@@ -26,6 +26,12 @@ TYPES = {
     "iq2_s": (GT.IQ2_S, FT.MOSTLY_IQ2_S, True, True),
     "iq3_xxs": (GT.IQ3_XXS, FT.MOSTLY_IQ3_XXS, True, True),
     "iq3_s": (GT.IQ3_S, FT.MOSTLY_IQ3_S, False, True),
+    # no kernel in the reference (its policy selects them: kernels/scheme.py:375, :521-523);
+    # like its Q4_0 they ignore importance weights
+    "q4_1": (GT.Q4_1, FT.MOSTLY_Q4_1, False, False),
+    "q5_0": (GT.Q5_0, FT.MOSTLY_Q5_0, False, False),
+    "q5_1": (GT.Q5_1, FT.MOSTLY_Q5_1, False, False),
+    "q8_0": (GT.Q8_0, FT.MOSTLY_Q8_0, False, False),
 }
 
 

@@ -25,7 +25,7 @@ def test_header_declares_the_boundary():
     names = declared_functions()
     for n in ("qs_quantize", "qs_init", "qs_row_bytes", "qs_block_info", "qs_last_error",
               "qs_type_supported", "qs_type_needs_qw", "qs_version", "qs_dequantize", "qs_block_error",
-              "qs_tensor_error"):
+              "qs_tensor_error", "qs_tensor_error_noalloc", "qs_device_fault"):
         assert n in names
 
 
@@ -43,7 +43,7 @@ def test_version():
 
 
 @pytest.mark.parametrize("name", ["Q4_0", "Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "IQ4_XS",
-                                  "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S"])
+                                  "IQ2_XXS", "IQ2_XS", "IQ2_S", "IQ3_XXS", "IQ3_S", "Q4_1", "Q5_0", "Q5_1", "Q8_0"])
 def test_block_geometry_matches_gguf(name):
     from gguf import GGMLQuantizationType as GT
     gt = GT[name]
@@ -55,13 +55,13 @@ def test_block_geometry_matches_gguf(name):
 
 def test_needs_qw_flags():
     L = _native.lib()
-    assert [t for t in (2, 10, 11, 12, 13, 14, 16, 17, 18, 21, 22, 23) if L.qs_type_needs_qw(t)] == [16, 17, 22]
+    assert [t for t in (2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 16, 17, 18, 21, 22, 23) if L.qs_type_needs_qw(t)] == [16, 17, 22]
 
 
 def test_argument_errors():
     L = _native.lib()
     with pytest.raises(_native.QsError) as e:
-        _native.row_bytes(7, 256)                      # Q5_1: not implemented
+        _native.row_bytes(20, 256)                     # IQ4_NL: not implemented
     assert e.value.code == _native.QS_ENOTSUP
     with pytest.raises(_native.QsError) as e:
         _native.row_bytes(12, 300)                     # not a multiple of 256
@@ -86,7 +86,7 @@ def test_decode_argument_errors():
     assert L.qs_dequantize(12, None, 144, 4, 250, None, 256, None) == _native.QS_EINVAL   # k % 256
     assert L.qs_dequantize(12, None, 100, 4, 256, None, 256, None) == _native.QS_EINVAL   # row stride
     assert L.qs_dequantize(12, None, 144, 4, 256, None, 255, None) == _native.QS_EINVAL   # dst stride
-    assert L.qs_dequantize(7, None, 144, 4, 256, None, 256, None) == _native.QS_ENOTSUP
+    assert L.qs_dequantize(20, None, 144, 4, 256, None, 256, None) == _native.QS_ENOTSUP
     assert L.qs_dequantize(12, None, 144, 0, 256, None, 256, None) == _native.QS_OK       # nothing to do
     assert L.qs_block_error(12, None, 144, None, 5, 4, 256, None, None, None) == _native.QS_EINVAL
     assert L.qs_block_error(12, None, 144, None, 30, 0, 256, None, None, None) == _native.QS_OK

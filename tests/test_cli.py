@@ -17,7 +17,8 @@ from synth_gguf import write_imatrix, write_llama, write_mixed
 CLI = str(PKG / "quant-studio.py")
 ORACLE_NAMES = {GT.Q4_0: "q4_0", GT.Q2_K: "q2_k", GT.Q3_K: "q3_k", GT.Q4_K: "q4_k", GT.Q5_K: "q5_k",
                 GT.Q6_K: "q6_k", GT.IQ4_XS: "iq4_xs", GT.IQ2_XXS: "iq2_xxs", GT.IQ2_XS: "iq2_xs",
-                GT.IQ2_S: "iq2_s", GT.IQ3_XXS: "iq3_xxs", GT.IQ3_S: "iq3_s"}
+                GT.IQ2_S: "iq2_s", GT.IQ3_XXS: "iq3_xxs", GT.IQ3_S: "iq3_s", GT.Q4_1: "q4_1", GT.Q5_0: "q5_0",
+                GT.Q5_1: "q5_1", GT.Q8_0: "q8_0"}
 
 
 def run(*args, check=True):
@@ -44,7 +45,7 @@ def test_errors(tmp_path):
     write_llama(src)
     r = run(src, tmp_path / "o.gguf", "IQ2_XXS", check=False)
     assert r.returncode != 0 and "importance matrix" in r.stderr
-    r = run(src, tmp_path / "o.gguf", "Q8_0", check=False)
+    r = run(src, tmp_path / "o.gguf", "IQ1_S", check=False)
     assert r.returncode != 0 and "not supported" in r.stderr
     r = run(src, tmp_path / "o.gguf", "NOPE", check=False)
     assert r.returncode != 0 and "unknown quantization scheme" in r.stderr
@@ -91,7 +92,7 @@ def _check_against_oracle(dst, vals, imat):
         name = ORACLE_NAMES[t.tensor_type]
         if qw is None and name in ("iq2_xxs", "iq2_xs", "iq2_s"):
             continue
-        if name == "q4_0":
+        if name in ("q4_0", "q4_1", "q5_0", "q5_1", "q8_0"):  # these ignore importance weights
             qw = None
         ref = oracle.quantize(name, x, None if qw is None else qw[: x.shape[1]])
         assert np.array_equal(np.asarray(t.data).reshape(ref.shape), ref), f"{t.name} ({name})"
@@ -107,6 +108,43 @@ def test_mixture_end_to_end_vs_oracle(tmp_path, scheme_name):
     imat = write_imatrix(im, {k: v.shape[1] for k, v in vals.items()})
     run(src, dst, scheme_name, "--imatrix", im, "--mem", "256K")
     assert _check_against_oracle(dst, vals, imat) >= 10
+
+
+def _plan(r):
+    lines = [l for l in r.stdout.splitlines() if " -> " in l and not l.startswith("dry run")]
+    return {l.split()[0]: l.split()[3] for l in lines}
+
+
+def test_dry_run_plans_the_formats_the_reference_rejects(tmp_path):
+    """The policy's Q5_0 / Q5_1 / Q8_0 shape fallbacks (scheme.py:375) and the Q4_1 ffn_down of
+    Q4_0 with an imatrix (scheme.py:521-523) plan and run here; the reference stops on them
+    (quant-studio.py:396-399)."""
+    src, im = tmp_path / "m.gguf", tmp_path / "im.gguf"
+    vals = write_llama(src, hidden=288)                  # rows of 288: not a multiple of 256
+    write_imatrix(im, {k: v.shape[1] for k, v in vals.items()})
+    plan = _plan(run(src, tmp_path / "o.gguf", "Q4_K_M", "--dry-run"))
+    assert plan["blk.0.attn_q.weight"] == "Q5_0" and plan["blk.1.attn_v.weight"] == "Q8_0"
+    plan = _plan(run(src, tmp_path / "o.gguf", "Q5_K_M", "--dry-run"))
+    assert plan["blk.0.attn_q.weight"] == "Q5_1"
+    src8 = tmp_path / "m8.gguf"
+    vals = write_llama(src8, n_layer=8)
+    write_imatrix(im, {k: v.shape[1] for k, v in vals.items()})
+    plan = _plan(run(src8, tmp_path / "o.gguf", "Q4_0", "--imatrix", im, "--dry-run"))
+    assert plan["blk.0.ffn_down.weight"] == "Q4_1" and plan["blk.1.ffn_down.weight"] == "Q4_0"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("scheme_name,hidden,n_layer", [("Q4_K_M", 288, 2), ("Q5_K_M", 288, 2), ("Q4_0", 256, 8),
+                                                        ("Q5_0", 256, 8), ("Q8_0", 256, 2)])
+def test_fallback_formats_end_to_end_vs_oracle(tmp_path, scheme_name, hidden, n_layer):
+    src, dst, im = tmp_path / "in.gguf", tmp_path / "out.gguf", tmp_path / "im.gguf"
+    vals = write_llama(src, hidden=hidden, n_layer=n_layer)
+    imat = write_imatrix(im, {k: v.shape[1] for k, v in vals.items()})
+    run(src, dst, scheme_name, "--imatrix", im, "--mem", "256K")
+    types = {t.tensor_type for t in GGUFReader(dst).tensors}
+    want = {"Q4_K_M": GT.Q5_0, "Q5_K_M": GT.Q5_1, "Q4_0": GT.Q4_1, "Q5_0": GT.Q5_1, "Q8_0": GT.Q8_0}[scheme_name]
+    assert want in types
+    assert _check_against_oracle(dst, vals, imat) >= 8
 
 
 @pytest.mark.gpu

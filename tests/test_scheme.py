@@ -61,7 +61,8 @@ def test_requires_imatrix():
 
 def test_scheme_table_marks_supported():
     table = scheme.format_scheme_table()
-    for name in ("Q4_K_M", "IQ2_XXS", "Q6_K", "IQ3_XXS", "IQ2_M", "Q4_0", "IQ4_XS"):
+    for name in ("Q4_K_M", "IQ2_XXS", "Q6_K", "IQ3_XXS", "IQ2_M", "Q4_0", "IQ4_XS", "Q4_1", "Q5_0", "Q5_1", "Q8_0"):
         assert scheme.parse_scheme(name).supported, name
         assert f"[x] {name}" in table
-    assert not scheme.parse_scheme("Q8_0").supported
+    for name in ("IQ1_S", "TQ1_0", "IQ4_NL"):
+        assert not scheme.parse_scheme(name).supported, name

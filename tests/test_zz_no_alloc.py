@@ -81,7 +81,7 @@ def test_noalloc_argument_errors():
     out = torch.zeros(2, dtype=torch.float64, device="cuda")
     assert L.qs_tensor_error_noalloc(12, None, 144, None, 30, 4, 250, None, out.data_ptr(), None) == nat.QS_EINVAL
     assert L.qs_tensor_error_noalloc(12, None, 144, None, 30, 4, 256, None, None, None) == nat.QS_EINVAL
-    assert L.qs_tensor_error_noalloc(7, None, 144, None, 30, 4, 256, None, out.data_ptr(), None) == nat.QS_ENOTSUP
+    assert L.qs_tensor_error_noalloc(20, None, 144, None, 30, 4, 256, None, out.data_ptr(), None) == nat.QS_ENOTSUP
     # empty tensor: sums are zero
     assert L.qs_tensor_error_noalloc(12, None, 144, None, 30, 0, 256, None, out.data_ptr(), None) == 0
     torch.cuda.synchronize()
