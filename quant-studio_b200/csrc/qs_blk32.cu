@@ -100,8 +100,6 @@ __device__ __forceinline__ int chunk_off(int R, int c) {
 }
 
 // --- per-block arithmetic ----------------------------------------------------------------
-// floor(v) for v in [0, 2^22): the low byte of v + 2^23 added rounding toward -infinity.
-__device__ __forceinline__ uint32_t floor_byte(float v) { return (uint32_t)__float_as_int(__fadd_rd(v, 8388608.0f)); }
 // Low bytes of four words -> one word (a in byte 0).
 __device__ __forceinline__ uint32_t pack4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -190,67 +188,66 @@ __device__ __forceinline__ float keep_lt(float v, float a) {
     return r;
 }
 
-// Value i (block order) of the block in stage row R, read from shared memory. The rare
-// paths below re-read the block this way and are kept out of line (__noinline__), so that
-// the common path carries none of their instructions.
+// Signed value of the first largest |x| (argmax of |x|, first index): max and min decide
+// it unless both +a and -a occur, or the block is all zeros (the first zero's sign).
 template <int SRC>
-__device__ __forceinline__ float stage_value(const uint8_t* stage, int R, int i) {
-    constexpr int ES = es_of<SRC>(), VPC = 16 / ES;
-    const uint8_t* p = stage + chunk_off<ES>(R, i / VPC) + (i % VPC) * ES;
-    if constexpr (SRC == SRC_F32) return *reinterpret_cast<const float*>(p);
-    const uint16_t h = *reinterpret_cast<const uint16_t*>(p);
-    if constexpr (SRC == SRC_BF16) return __uint_as_float((uint32_t)h << 16);
-    else return __half2float(__ushort_as_half(h));
-}
-
-// argmax of |x| (first index) and the signed value there.
-template <int SRC>
-__device__ __noinline__ float absmax_scan(const uint8_t* stage, int R) {
-    float m = stage_value<SRC>(stage, R, 0), am = fabsf(m);
+__device__ __forceinline__ float first_absmax(float mx, float mn, const Blk<SRC>& B) {
+    if (mx != -mn) return mx > -mn ? mx : mn;
+    float m = B.at(0), am = fabsf(m);
+#pragma unroll
     for (int i = 1; i < 32; i++) {
-        const float v = stage_value<SRC>(stage, R, i);
-        if (fabsf(v) > am) { am = fabsf(v); m = v; }
+        const float v = B.at(i);
+        const bool gt = fabsf(v) > am;
+        am = gt ? fabsf(v) : am;
+        m = gt ? v : m;
     }
     return m;
 }
 
-// Signed value of the first largest |x|: max and min decide it unless both +a and -a occur,
-// or the block is all zeros (then the first zero's sign counts).
+// ggml's scalar max / min (`if (v > max) max = v`, the first of tied values kept): only the
+// sign of a zero result can differ from the order-free trees, so the scalar loop runs only
+// when a result is zero.
 template <int SRC>
-__device__ __forceinline__ float first_absmax(float mx, float mn, const uint8_t* stage, int R) {
-    return mx != -mn ? (mx > -mn ? mx : mn) : absmax_scan<SRC>(stage, R);
-}
-
-// ggml's scalar max / min (`if (v > max) max = v`, first of tied values kept).
-template <int SRC>
-__device__ __noinline__ float2 max_min_scan(const uint8_t* stage, int R) {
-    float a = stage_value<SRC>(stage, R, 0), b = a;
+__device__ __forceinline__ void first_max_min(float& mx, float& mn, const Blk<SRC>& B) {
+    if (mx != 0.0f && mn != 0.0f) return;
+    float a = B.at(0), b = a;
+#pragma unroll
     for (int i = 1; i < 32; i++) {
-        const float v = stage_value<SRC>(stage, R, i);
+        const float v = B.at(i);
         a = keep_gt(v, a);
         b = keep_lt(v, b);
     }
-    return make_float2(a, b);
+    mx = a;
+    mn = b;
 }
 
-// Only the sign of a zero result can differ between ggml's loop and the order-free trees,
-// so the loop runs only when a result is zero.
-template <int SRC>
-__device__ __forceinline__ void first_max_min(float& mx, float& mn, const uint8_t* stage, int R) {
-    if (mx != 0.0f && mn != 0.0f) return;
-    const float2 r = max_min_scan<SRC>(stage, R);
-    mx = r.x;
-    mn = r.y;
+// --- packing on the FMA pipe ----------------------------------------------------------------
+// The level bytes come out of floor_bits as 0x4B000000 + n (n < 256). Multiplying by 2^8,
+// 2^16 or 2^24 modulo 2^32 drops the 0x4B000000 term, so four levels pack into one word with
+// integer multiply-adds (IMAD, FMA pipe) instead of byte permutes on the ALU pipe.
+// floor(v) for v in [0, 2^23): v + 2^23 added rounding toward -infinity is the float
+// 2^23 + floor(v), whose bits are 0x4B000000 + floor(v).
+__device__ __forceinline__ uint32_t floor_bits(float v) { return (uint32_t)__float_as_int(__fadd_rd(v, 8388608.0f)); }
+__device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
 }
-
-// Q4_0 levels k * 4 .. k * 4 + 3 of a block whose id is infinite: torch's clamp + uint8
-// cast of floor(x * id + 8.5) (+inf -> 15, -inf and NaN -> 0), one byte each.
-template <int SRC>
-__device__ __noinline__ uint32_t q4_0_inf_word(const uint8_t* stage, int R, float id, int k) {
-    uint32_t w = 0;
-    for (int j = 0; j < 4; j++)
-        if (stage_value<SRC>(stage, R, 4 * k + j) * id + 8.5f == INFINITY) w |= 15u << (8 * j);
-    return w;
+__device__ __forceinline__ uint32_t mul_hi(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+// bytes n0 | n1 << 8 | n2 << 16 | n3 << 24 from four floor_bits results
+__device__ __forceinline__ uint32_t pack_levels(uint32_t f0, uint32_t f1, uint32_t f2, uint32_t f3) {
+    return mad_lo(f3, 1u << 24, mad_lo(f2, 1u << 16, mad_lo(f1, 1u << 8, f0 - 0x4B000000u)));
+}
+// qs words of the 4-bit formats from the low (values j) and high (values j + 16) level words
+// whose bytes are <= 16: clamp each byte to 15 and combine, lo + 16 * hi with the 16s taken
+// out: lo - ((lo & 0x10..) >> 4) + 16 * hi - (hi & 0x10..).
+__device__ __forceinline__ uint32_t qs_clamp16(uint32_t lo, uint32_t hi) {
+    const uint32_t t = lo & 0x10101010u, u = hi & 0x10101010u;
+    return mad_lo(hi, 16u, lo) - mul_hi(t, 1u << 28) - u;
 }
 
 template <int BB>
@@ -296,27 +293,36 @@ __device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint
         // x * id + off infinite or NaN: the levels then follow the casts of the two
         // references, torch's clamp + uint8 for Q4_0 (+inf -> 15, -inf / NaN -> 0) and ggml's
         // / numpy's int cast for Q5_0 (0).
-        const float m = first_absmax<SRC>(mx, mn, stage, R);
+        const float m = first_absmax<SRC>(mx, mn, B);
         const float d = QT == QS_Q4_0 ? m * -0.125f : m * -0.0625f;
         const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
         constexpr float off = QT == QS_Q4_0 ? 8.5f : 16.5f;
-        constexpr int top = QT == QS_Q4_0 ? 4 : 5;
+        uint32_t qs[4];
         if (!isinf(id)) {
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint32_t w = pack4(floor_byte(B.at(4 * k) * id + off), floor_byte(B.at(4 * k + 1) * id + off),
-                                         floor_byte(B.at(4 * k + 2) * id + off), floor_byte(B.at(4 * k + 3) * id + off));
-                W[k] = w - ((w >> top) & 0x01010101u);
-            }
-        } else if constexpr (QT == QS_Q4_0) {
+            for (int k = 0; k < 8; k++)
+                W[k] = pack_levels(floor_bits(B.at(4 * k) * id + off), floor_bits(B.at(4 * k + 1) * id + off),
+                                   floor_bits(B.at(4 * k + 2) * id + off), floor_bits(B.at(4 * k + 3) * id + off));
+            if constexpr (QT == QS_Q4_0) {
 #pragma unroll
-            for (int k = 0; k < 8; k++) W[k] = q4_0_inf_word<SRC>(stage, R, id, k);
+                for (int j = 0; j < 4; j++) qs[j] = qs_clamp16(W[j], W[j + 4]);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 8; k++) W[k] -= mul_hi(W[k] & 0x20202020u, 1u << 27);  // 32 -> 31
+                nibbles(W, qs);
+            }
         } else {
 #pragma unroll
-            for (int k = 0; k < 8; k++) W[k] = 0u;
+            for (int k = 0; k < 8; k++) {
+                uint32_t w = 0;
+                if constexpr (QT == QS_Q4_0) {
+#pragma unroll
+                    for (int j = 0; j < 4; j++) w |= (B.at(4 * k + j) * id + off == INFINITY ? 15u : 0u) << (8 * j);
+                }
+                W[k] = w;
+            }
+            nibbles(W, qs);
         }
-        uint32_t qs[4];
-        nibbles(W, qs);
         const uint32_t dh = f16_bits(d);
         if constexpr (QT == QS_Q4_0) {  // [d][qs 16]
             rec[0] = dh | (qs[0] << 16);
@@ -337,16 +343,21 @@ __device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint
         // few ulps, so the floors never exceed nmax; an infinite id (d below 2^-128) makes
         // every level inf / NaN, which the int cast of the references turns into 0: an id of
         // 0 gives those zeros through the same arithmetic.
-        first_max_min<SRC>(mx, mn, stage, R);
+        first_max_min<SRC>(mx, mn, B);
         const float d = __fdiv_rn(mx - mn, QT == QS_Q4_1 ? 15.0f : 31.0f);
         float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
         id = isinf(id) ? 0.0f : id;
 #pragma unroll
         for (int k = 0; k < 8; k++)
-            W[k] = pack4(floor_byte((B.at(4 * k) - mn) * id + 0.5f), floor_byte((B.at(4 * k + 1) - mn) * id + 0.5f),
-                         floor_byte((B.at(4 * k + 2) - mn) * id + 0.5f), floor_byte((B.at(4 * k + 3) - mn) * id + 0.5f));
+            W[k] = pack_levels(floor_bits((B.at(4 * k) - mn) * id + 0.5f), floor_bits((B.at(4 * k + 1) - mn) * id + 0.5f),
+                               floor_bits((B.at(4 * k + 2) - mn) * id + 0.5f), floor_bits((B.at(4 * k + 3) - mn) * id + 0.5f));
         uint32_t qs[4];
-        nibbles(W, qs);
+        if constexpr (QT == QS_Q4_1) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) qs[j] = mad_lo(W[j + 4], 16u, W[j]);  // levels <= 15
+        } else {
+            nibbles(W, qs);
+        }
         rec[0] = f16_bits(d) | ((uint32_t)f16_bits(mn) << 16);
         if constexpr (QT == QS_Q4_1) {  // [d][m][qs 16]
 #pragma unroll
