@@ -359,6 +359,9 @@ def main() -> None:
             q = None if qw is None else torch.from_numpy(qw).to(device)
             return _native.quantize(gt, xd, q).cpu().numpy()
         line["cpu_baseline"] = cpu_baseline(args, gpu_quantize)
+        pv = parity_vs_reference(args, gpu_quantize)
+        if pv is not None:
+            line["cpu_baseline"]["vs_reference"] = pv
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
@@ -688,6 +691,34 @@ def e2e_bench(torch, _native, gt, xs, qws, outs, device, args, dist, allmax, wor
             "copy_ceiling": {"value": round(ceiling, 3), "unit": "GB/s", "ms_per_step": round(ms_copy, 3),
                              "what": "the same H2D / D2H copies and chunking with no kernels, all ranks at once"},
             "frac_of_copy_ceiling": round(value / ceiling, 4)}
+
+
+def parity_vs_reference(args, gpu_quantize) -> dict | None:
+    """Identical-block fraction of the GPU output against the reference as shipped on the
+    configs[1] row subsets of tests/golden/config_parity.json (the reference's own outputs):
+    the GPU bytes must hash like the reference with a correctly rounded sqrt; the shipped
+    reference then differs exactly in the blocks the fixture lists."""
+    import hashlib
+    fix_path = ROOT / "tests" / "golden" / "config_parity.json"
+    if not fix_path.exists():
+        return None
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import config_rows
+    cases = [c for c in json.loads(fix_path.read_text())["cases"].values()
+             if c["type"] == args.qtype and c["case"] in ("c2_a", "c2_b") and c["imatrix"] == args.imatrix]
+    if not cases:
+        return None
+    blocks = differ = 0
+    exact = True
+    for c in cases:
+        x = config_rows.rows_f32(c["case"])
+        got = gpu_quantize(x, config_rows.imatrix(x.shape[1]) if c["imatrix"] else None)
+        exact &= hashlib.sha256(got.tobytes()).hexdigest() == c["sha_ieee"]
+        blocks += c["blocks"]
+        differ += len(c["diff"])
+    return {"identical_blocks_vs_reference": round(1.0 - differ / blocks, 6) if exact else None,
+            "bit_exact_vs_ieee_sqrt_reference": exact, "blocks_compared": blocks,
+            "sample": "first rows of the configs[1] tensors (tests/golden/config_parity.json)"}
 
 
 def cpu_baseline(args, gpu_quantize=None) -> dict:
