@@ -150,8 +150,115 @@ def make_inputs(torch, device, seed: int, shapes):
     return xs, qws
 
 
+REF_DIR = ROOT / "baseline" / "_ref" / "quant-studio"
+# the reference's entry point per type: (module, function) in its kernels package
+REF_FUNCS = {"q4_0": ("q4_0", "quantize_q4_0"), "q2_k": ("q2_k", "quantize_q2_k"), "q3_k": ("q3_k", "quantize_q3_k"),
+             "q4_k": ("q4_k", "quantize_q4_k"), "q5_k": ("q5_k", "quantize_q5_k"), "q6_k": ("q6_k", "quantize_q6_k"),
+             "iq4_xs": ("iq4_xs", "quantize_iq4_xs"), "iq2_xxs": ("iq2", "quantize_iq2_xxs"),
+             "iq2_xs": ("iq2_xs", "quantize_iq2_xs"), "iq2_s": ("iq2_s", "quantize_iq2_s"),
+             "iq3_xxs": ("iq3_xxs", "quantize_iq3_xxs"), "iq3_s": ("iq3_s", "quantize_iq3_s")}
+
+
+def reference_quantizer(qtype: str):
+    """The reference's own quantize_<type>, imported unmodified from its copy in baseline/_ref
+    (its GPU path: torch ops on CUDA plus its Triton kernels; its CPU path: torch eager). pip
+    gguf 0.19 lacks two enum members the reference's policy module names (GGMLQuantizationType
+    .Q2_0, LlamaFileType.MOSTLY_Q2_0); they are added first, as placeholders, so that its
+    package imports. Returns None when the copy is absent."""
+    if not REF_DIR.exists() or qtype not in REF_FUNCS:
+        return None
+    from gguf import GGMLQuantizationType as GT
+    from gguf.constants import LlamaFileType as FT
+
+    def add(cls, name, value):
+        if hasattr(cls, name):
+            return
+        m = int.__new__(cls, value)
+        m._name_, m._value_ = name, value
+        type.__setattr__(cls, name, m)
+        cls._member_map_[name] = m
+        cls._value2member_map_[value] = m
+        cls._member_names_.append(name)
+
+    add(FT, "MOSTLY_Q2_0", 1000)
+    add(GT, "Q2_0", 1000)
+    sys.dont_write_bytecode = True
+    sys.path[:] = [p for p in sys.path if not p.rstrip("/").endswith("quant-studio_b200")]
+    sys.path.insert(0, str(REF_DIR))
+    import importlib
+    mod, fn = REF_FUNCS[qtype]
+    return getattr(importlib.import_module(f"kernels.{mod}"), fn)
+
+
+def reference_torch_cpu(args, fn, qw_np, sample) -> dict:
+    """The reference's own CPU path (torch eager, all host threads) on a bounded sample."""
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    qw = None if qw_np is None else torch.from_numpy(qw_np)
+
+    def call(a):
+        xt = torch.from_numpy(a)
+        return fn(xt) if args.qtype == "q4_0" else fn(xt, qw)
+
+    call(sample(8))
+    probe = sample(64)
+    t0 = time.perf_counter()
+    call(probe)
+    rate = probe.size / max(time.perf_counter() - t0, 1e-6)
+    rows = int(min(4096, max(64, rate * 4.0 / probe.shape[1])))
+    x = sample(rows)
+    t0 = time.perf_counter()
+    call(x)
+    dt = time.perf_counter() - t0
+    return {"value": round(x.size * 2 / dt / 1e9, 6), "unit": "GB/s", "cores": cores,
+            "torch_threads": torch.get_num_threads(), "kind": "reference (torch eager CPU path, unmodified)",
+            "sample": f"{rows} rows x {x.shape[1]} values ({x.size * 2 / 1e6:.1f} MB bf16), {dt:.2f} s"}
+
+
+def reference_gpu(args, fn) -> dict:
+    """The reference's own GPU path (torch ops on CUDA + its Triton kernels), unmodified, on the
+    same workload and device as the qsb200 arm: device-resident bf16 tensors, upcast to float32
+    as its pipeline does (quant-studio.py:197), then quant_fn; CUDA events around each step."""
+    import torch
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    xs, qws = make_inputs(torch, device, seed=0, shapes=SHAPES_C2)
+    if not args.imatrix or args.qtype == "q4_0":
+        qws = [None] * len(xs)
+
+    def step():
+        outs = []
+        for x, q in zip(xs, qws):
+            xf = x.to(torch.float32)
+            outs.append(fn(xf) if args.qtype == "q4_0" else fn(xf, q))
+        return outs
+
+    t0 = time.perf_counter()
+    step()                               # Triton JIT compiles here
+    torch.cuda.synchronize()
+    compile_s = time.perf_counter() - t0
+    for _ in range(max(1, args.warmup - 1)):
+        step()
+    torch.cuda.synchronize()
+    steps = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    n = sum(r * c for r, c in SHAPES_C2)
+    return {"value": round(2 * n / (ms * 1e-3) / 1e9, 4), "unit": "GB/s", "ms_per_step": round(ms, 3),
+            "steps": steps, "first_step_s": round(compile_s, 2),
+            "kind": "reference GPU path (torch + Triton, unmodified), same B200, device-resident bf16 inputs "
+                    "upcast to f32 as its pipeline does", "device": torch.cuda.get_device_name(device)}
+
+
 def run_reference(args, config: dict) -> None:
-    """The reference arm: the CPU port of the reference algorithm on all host threads."""
+    """The reference arm: the CPU port of the reference algorithm on all host threads, with the
+    reference's own CPU path and its GPU path on the same box beside it."""
     import oracle
 
     cores = os.cpu_count() or 1
@@ -182,6 +289,24 @@ def run_reference(args, config: dict) -> None:
         times.append(time.perf_counter() - t0)
     dt = statistics.median(times)
     gbs = x.size * 2 / dt / 1e9
+    extra = {}
+    ref_fn = None
+    try:
+        ref_fn = reference_quantizer(args.qtype)
+    except Exception as e:  # the unmodified reference failed to import
+        extra["reference_import_error"] = f"{type(e).__name__}: {e}"[:300]
+    if ref_fn is not None:
+        try:
+            extra["reference_torch_cpu"] = reference_torch_cpu(args, ref_fn, qw if args.imatrix else None, sample)
+        except Exception as e:
+            extra["reference_torch_cpu"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        if args.ref_gpu:
+            try:
+                extra["reference_gpu"] = reference_gpu(args, ref_fn)
+            except Exception as e:
+                extra["reference_gpu"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    elif "reference_import_error" not in extra:
+        extra["reference_torch_cpu"] = {"unavailable": f"no copy of the reference at {REF_DIR.relative_to(ROOT)}"}
     line = {"impl": "reference", "value": round(gbs, 6),
             "metric": f"input GB/s quantized (bf16->{args.qtype}{', imatrix' if args.imatrix else ''})",
             "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -191,6 +316,7 @@ def run_reference(args, config: dict) -> None:
                              "sample": f"{rows} rows x {k} bf16 values per step ({x.size * 2 / 1e6:.1f} MB) "
                                        f"of the benchmark distribution, median of {args.steps} steps"},
             "e2e": {"value": round(gbs, 6), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    line.update(extra)
     print(json.dumps(line), flush=True)
 
 
@@ -203,6 +329,8 @@ def main() -> None:
     ap.add_argument("--qtype", default="q4_k")
     ap.add_argument("--no-imatrix", dest="imatrix", action="store_false")
     ap.add_argument("--ref-seconds", type=float, default=1.0, help="CPU seconds per reference step")
+    ap.add_argument("--no-ref-gpu", dest="ref_gpu", action="store_false",
+                    help="--impl reference: skip timing the reference's own GPU path")
     ap.add_argument("--no-e2e", dest="e2e", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--op", default="quantize", choices=["quantize", "dequantize", "tensor_error", "cli"],
