@@ -80,6 +80,13 @@ __device__ __forceinline__ float clamp_nan(float x, float lo, float hi) {
     asm("{.reg .f32 t; max.NaN.f32 t, %1, %2; min.NaN.f32 %0, t, %3;}" : "=f"(r) : "f"(x), "f"(lo), "f"(hi));
     return r;
 }
+// rintf(v) (ties to even) for the candidate loops, as two adds on the FMA pipe instead of a
+// round instruction on the slower XU pipe: v + 1.5 * 2^23 lands in [2^23, 2^24), where the
+// spacing is 1, so the add rounds v to an integer (ties to even, as 1.5 * 2^23 is even) and
+// the subtraction is exact. Equal to rintf for |v| < 2^22 except that a zero result is +0;
+// beyond that it stays beyond +-(2^22 - 1), so a following clamp to a small level range gives
+// the same level for every finite v; inf and NaN pass through.
+__device__ __forceinline__ float rint_add(float v) { return __fadd_rn(__fadd_rn(v, 12582912.0f), -12582912.0f); }
 __device__ __forceinline__ uint16_t f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
 __device__ __forceinline__ float f16_val(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 

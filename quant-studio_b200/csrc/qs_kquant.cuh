@@ -43,7 +43,7 @@ __device__ __forceinline__ float qkx_search(const float* x, const float* w, cons
         float la[N], wl[N], wl2[N], wlx[N];
 #pragma unroll
         for (int i = 0; i < N; i++) {
-            la[i] = clamp_nan(rintf(isc * (x[i] - mn)), 0.0f, fmax);
+            la[i] = clamp_nan(rint_add(isc * (x[i] - mn)), 0.0f, fmax);
             wl[i] = w[i] * la[i];
             wl2[i] = wl[i] * la[i];
             wlx[i] = wl[i] * x[i];
@@ -306,7 +306,7 @@ __device__ __forceinline__ float qx_search(const float* x, const float* w, float
         float slx = 0.0f, sl2 = 0.0f;
 #pragma unroll
         for (int i = 0; i < N; i++) {
-            const float la = clampf(rintf(isc * x[i]), -fmax, fmax - 1.0f);
+            const float la = clampf(rint_add(isc * x[i]), -fmax, fmax - 1.0f);
             const float a = wx[i] * la, b = (w[i] * la) * la;
             slx = i == 0 ? a : slx + a;
             sl2 = i == 0 ? b : sl2 + b;
