@@ -457,9 +457,14 @@ def main() -> None:
                                  "ops_per_value": ops, "frac": round(lane_ach / lane_peak, 4)}
     prof = ROOT / "profiles" / f"traffic_{args.qtype}{'_imat' if args.imatrix else ''}.json"
     if prof.exists():
-        roof["traffic"] = json.loads(prof.read_text()).get("bytes_per_value_launch")
+        counters = json.loads(prof.read_text())
+        roof["traffic"] = counters.get("bytes_per_value_launch")
         if roof["traffic"] is not None:
             roof["traffic"] = round(roof["traffic"] * elems_per_launch)
+        # executed work beside the frozen algorithmic count: ncu's thread instructions per value
+        # on one 14336 x 4096 launch of this kernel (profiles/traffic_<type>.json)
+        if counters.get("thread_inst_per_value") is not None:
+            roof["inst_per_value_ncu"] = counters["thread_inst_per_value"]
 
     # end to end through the public API from pinned host memory
     e2e = None
@@ -548,13 +553,21 @@ def bench_config1(torch, _native, device, args, info) -> dict:
     ach = alg / (us * 1e-6) / 1e9
     ok = all(torch.equal(o, outs[0]) for o in outs[1:])
     del g
+    counters = ROOT / "profiles" / "traffic_q4_0.json"
+    traffic = inst = None
+    if counters.exists():  # ncu DRAM bytes per value of one 14336 x 4096 launch, scaled to this one
+        c = json.loads(counters.read_text())
+        traffic = round(c["bytes_per_value_launch"] * rows * cols)
+        inst = c.get("thread_inst_per_value")
     return {"workload": "BASELINE configs[0]: Q4_0, no imatrix, one 4096x4096 bf16 tensor (43.0 MB per launch); "
                         f"launches rotate over {R} copies (L2 cold for every launch)",
             "metric": "input GB/s quantized (bf16->q4_0)", "value": round(2 * rows * cols / (us * 1e-6) / 1e9, 2),
             "unit": "GB/s", "us_per_launch": round(us, 3), "launches": reps * R,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(ach / peaks["hbm_gbs"], 4), "bytes_per_value": 2 + 18 / 32,
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback"},
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if not peaks.get("fallback") else "fallback",
+                         "traffic": traffic, "traffic_note": "ncu DRAM bytes per value of a 14336 x 4096 launch x the "
+                                                             "values of this launch", "inst_per_value_ncu": inst},
             "copies_identical": ok, "clocks": clk.summary()}
 
 
