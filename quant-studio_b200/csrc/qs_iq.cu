@@ -487,7 +487,12 @@ __device__ __forceinline__ int iq_index(const float* xval, int q, float inv) {
     int idx = 0, mul = 1;
 #pragma unroll
     for (int j = 0; j < Tr::NPOS; j++) {
-        const int l = (int)clampf(rintf(0.5f * (inv * xval[q * Tr::NPOS + j] - 1.0f)), 0.0f, (float)Tr::MAXL);
+        // clamp(rint(u), 0, MAXL) as an integer without the round and convert instructions (XU
+        // pipe): u + 1.5 * 2^23 rounds u to an integer in the low mantissa bits (|u| is a few
+        // units here); u is first raised to -1, which changes no level and sends NaN to 0 as
+        // the float-to-int conversion did
+        const float u = fmaxf(0.5f * (inv * xval[q * Tr::NPOS + j] - 1.0f), -1.0f);
+        const int l = min(max(__float_as_int(__fadd_rn(u, 12582912.0f)) - 0x4B400000, 0), Tr::MAXL);
         if (Tr::BITS == 2) { idx += l * mul; mul *= 3; }
         else idx |= l << (3 * j);
     }
@@ -520,7 +525,9 @@ __device__ __forceinline__ void iq_decode(const uint32_t* win, float* q) {
     for (int s = 0; s < Tr::NSUB; s++) {
         const int code = (int)(win[s] & 0xFFFF);
 #pragma unroll
-        for (int j = 0; j < Tr::NPOS; j++) q[s * Tr::NPOS + j] = (float)(2 * ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1)) + 1);
+        for (int j = 0; j < Tr::NPOS; j++)  // 2l + 1 as a float: the bits of 2^23 + 2l + 1, minus 2^23
+            q[s * Tr::NPOS + j] = __fadd_rn(__int_as_float(0x4B000001 + 2 * ((code >> (Tr::BITS * j)) & (Tr::NLEV - 1))),
+                                            -8388608.0f);
     }
 }
 
