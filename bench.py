@@ -14,16 +14,24 @@ only for the barrier and the max-over-ranks of the timings).
   value  input GB/s with inputs resident in HBM (whole job, all ranks)
   e2e    the same metric through the public API from pinned host buffers: per step every
          tensor is copied host->device, quantized and its blocks copied back to host, in
-         row chunks with the copies and kernels overlapped on three streams
+         row chunks with the copies and kernels overlapped on three streams; beside it the
+         same copies with no kernels, on every rank at once (`copy_ceiling`)
   roofline  the Q4_K kernel against the FP32 lane-op ceiling (148 SMs x 128 lanes x SM clock):
          algorithmic ops = 655 per value (37 x 17 per candidate step + 11 initial + 3 sums
-         + 5 weights + 7 requant/pack); plus the HBM view of the same launches
+         + 5 weights + 7 requant/pack); plus the HBM view of the same launches, and ncu's
+         DRAM bytes and thread instructions per value of one launch (profiles/traffic_*.json)
+  config1 / config3  (one GPU) BASELINE configs[0] (Q4_0 of one 4096 x 4096 tensor, against
+         HBM) and configs[2] (IQ2_XXS set + the 151936 x 2560 embedding as Q4_0)
 cpu_baseline  the CPU restatement of the reference's algorithm (oracle/) on all host cores over
          a bounded sample of the workload; the same sample is quantized on the GPU and
-         `identical_blocks` is the fraction of blocks that match (the metric's identical-block %)
+         `identical_blocks` is the fraction of blocks that match; `vs_reference`: the GPU
+         output on the configs[1] rows of tests/golden/config_parity.json against the
+         reference's own outputs there (identical-block fraction vs the shipped reference)
 --impl reference: the CPU restatement of the reference's algorithm (oracle/) on all host
-cores over a bounded sample of the same workload (the reference itself is Python/torch and
-cannot travel to the GPU host; oracle/ is its bit-exact C port).
+cores over a bounded sample of the same workload (the reference's eager code is Python and
+oracle/ is its bit-exact C port, about 10x faster than it); beside it, the reference itself
+from its copy in baseline/_ref: its torch CPU path on all host cores (`reference_torch_cpu`)
+and its GPU path (torch + Triton) on the same B200 and workload (`reference_gpu`).
 """
 
 from __future__ import annotations
