@@ -56,13 +56,13 @@ struct DeviceState {
     cudaMemPool_t pool = nullptr;  // scratch of qs_tensor_error; keeps its memory between calls
 };
 
-std::mutex g_mu;
+std::mutex g_mu[kMaxDevices];  // one per device: devices come up in parallel
 DeviceState g_dev[kMaxDevices];
 
 // Caller holds no lock; the device must be current.
 int ensure_device(int device, DeviceState** out) {
     if (device < 0 || device >= kMaxDevices) return fail(QS_EINVAL, "device %d out of range", device);
-    std::lock_guard<std::mutex> lk(g_mu);
+    std::lock_guard<std::mutex> lk(g_mu[device]);
     DeviceState& d = g_dev[device];
     if (!d.ready) {
         cudaError_t e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);

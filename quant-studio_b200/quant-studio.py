@@ -125,8 +125,8 @@ def pick_devices(device: str, ngpus: int) -> list[torch.device]:
 
 def start_device_warmup(args) -> tuple[threading.Thread, dict]:
     """Pick the devices, bring up their CUDA contexts and libqsb200 state and allocate the
-    pipeline's staging buffers on a background thread, while the main thread reads and plans
-    the model."""
+    pipeline's staging buffers on a background thread (the devices in parallel, one thread
+    each), while the main thread reads and plans the model."""
     box: dict = {}
 
     def run() -> None:
@@ -135,12 +135,25 @@ def start_device_warmup(args) -> tuple[threading.Thread, dict]:
             # a chunk holds at most CHUNK_BYTES of source rows; blocks are under half of that
             # from 16-bit sources (the pipeline grows the staging if a run needs more)
             in_bytes = min(ShardedQuantizer.CHUNK_BYTES, 16 * parse_mem(args.mem))
-            for d in devs:
-                torch.cuda.set_device(d)
-                torch.empty(1, device=d)
-                _native.check(_native.lib().qs_init(d.index))
-            for d in devs:
-                stage_buffers(d, in_bytes, in_bytes // 2)
+            errors: list[BaseException] = []
+
+            def up(d: torch.device) -> None:  # one device: context, library state, staging
+                try:
+                    torch.cuda.set_device(d)
+                    torch.empty(1, device=d)
+                    _native.check(_native.lib().qs_init(d.index))
+                    stage_buffers(d, in_bytes, in_bytes // 2)
+                except BaseException as e:
+                    errors.append(e)
+
+            torch.cuda.init()  # once, before the devices come up in parallel
+            ups = [threading.Thread(target=up, args=(d,), daemon=True) for d in devs]
+            for t in ups:
+                t.start()
+            for t in ups:
+                t.join()
+            if errors:
+                raise errors[0]
             box["devices"] = devs
         except BaseException as e:  # re-raised on the main thread
             box["error"] = e
