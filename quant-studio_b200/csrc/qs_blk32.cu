@@ -19,12 +19,19 @@
 //   * a persistent CTA owns one contiguous range of blocks; the ranges of all CTAs differ by
 //     at most 8 blocks and start at multiples of 8 blocks, so every warp's packed output
 //     starts on a 16-byte boundary;
-//   * a producer warp streams the range through a ring of NST shared-memory stages of 256
-//     blocks (cp.async.bulk.tensor, no multicast), each completing on the stage's `full`
-//     mbarrier; 8 consumer warps each take 32 blocks of a stage, one block per lane,
-//     release the stage on its `empty` mbarrier (the producer refills a slot once all 8
-//     warps released it) and store their 32 packed blocks from a per-warp staging with
-//     16-byte stores.
+//   * a producer warp streams the range through a ring of shared-memory stages
+//     (cp.async.bulk.tensor, no multicast), each completing on its `full` mbarrier; 8
+//     consumer warps quantize one block per lane, release the stage on its `empty`
+//     mbarrier and store their 32 packed blocks from a per-warp staging with 16-byte
+//     stores. Stages are G x 32 blocks shared by G warps: G = 8 (256-block stages that all
+//     warps read) for long ranges, G = 1 (32-block stages, stage j for warp j % 8) when a
+//     CTA has fewer than 8 of the large stages, where ramp and tail are a good part of the
+//     launch: every warp starts after a 2 KB copy, and the CTA ends one small stage after
+//     its last copy (measured: 4096 x 4096 Q4_0 12.0 -> 11.1 us, while 14336 x 4096 keeps
+//     the 256-block stages, 31.9 us against 35.0 us with small ones);
+//   * under programmatic stream serialization the next launch's CTAs set up while this
+//     grid's last CTAs finish; the producer waits for the previous grid before its first
+//     copy.
 // Every mbarrier wait is bounded: a wait that runs out records bit 0 of g_qs_fault_bits
 // (read by qs_device_fault) and the warp leaves instead of hanging the GPU.
 #include <cuda.h>  // CUtensorMap; the encoder is resolved at run time through the runtime
@@ -40,7 +47,6 @@ namespace {
 
 constexpr int B32_CW = 8;                         // consumer warps
 constexpr int B32_THREADS = (B32_CW + 1) * 32;    // + one producer warp
-constexpr int B32_BPS = B32_CW * 32;              // blocks (tensor rows) per stage
 constexpr int64_t B32_PIECE = int64_t(1) << 31;   // blocks per launch (tensor-map extent limit)
 
 template <int QT> struct B32;
@@ -50,16 +56,18 @@ template <> struct B32<QS_Q5_0> { static constexpr int BB = 22; };
 template <> struct B32<QS_Q5_1> { static constexpr int BB = 24; };
 template <> struct B32<QS_Q8_0> { static constexpr int BB = 34; };
 
-// Shared memory of one CTA: ring (1024-byte aligned stages), per-warp double-buffered output
-// staging, mbarriers. 16-bit sources: 3-4 stages of 16 KB within 75 KB, three CTAs per SM
-// (up to 192 KB of copies in flight per SM); f32: 3 stages of 32 KB, two CTAs per SM.
-template <int QT, int ES> struct B32Cfg {
-    static constexpr int STAGE = B32_BPS * 32 * ES;
+// Shared memory of one CTA: ring of 1024-byte aligned stages of G x 32 blocks, per-warp
+// double-buffered output staging, mbarriers. 16-bit sources: about 64 KB of stages within
+// 75 KB, three CTAs per SM (up to 192 KB of copies in flight per SM); f32: about 96 KB, two
+// CTAs per SM. G = 1 keeps a multiple of 8 slots, the same number for each warp.
+template <int QT, int ES, int G> struct B32Cfg {
+    static constexpr int ROWS = 32 * G;  // blocks per stage
+    static constexpr int STAGE = ROWS * 32 * ES;
     static constexpr int WST = (32 * B32<QT>::BB + 15) / 16 * 16;  // one warp's staging
     static constexpr int BUDGET = ES == 2 ? 75 * 1024 : 110 * 1024;
-    static constexpr int NST0 = (BUDGET - 2 * B32_CW * WST - 128) / STAGE;
-    static constexpr int NST = NST0 < 2 ? 2 : NST0;
-    static constexpr int BYTES = NST * STAGE + 2 * B32_CW * WST + 16 * NST;
+    static constexpr int N0 = (BUDGET - 2 * B32_CW * WST - 512) / STAGE;
+    static constexpr int NSLOT = G == 1 ? (N0 / 8 < 2 ? 16 : N0 / 8 * 8) : (N0 < 2 ? 2 : N0);
+    static constexpr int BYTES = NSLOT * STAGE + 2 * B32_CW * WST + 16 * NSLOT;
     static constexpr int MIN_CTAS = ES == 2 ? 3 : 2;
 };
 
@@ -71,7 +79,7 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(bar) : "memory");
 }
-// Rows [y, y + B32_BPS) of the block tensor into `dst` (the whole box is always written:
+// The box of rows [y, ...) of the block tensor into `dst` (the whole box is always written:
 // rows past the tensor's end are zero-filled), completing `bytes` on the barrier.
 __device__ __forceinline__ void tensor_load(uint32_t dst, const CUtensorMap* map, int y, uint32_t bytes, uint32_t bar) {
     asm volatile(
@@ -250,14 +258,27 @@ __device__ __forceinline__ uint32_t qs_clamp16(uint32_t lo, uint32_t hi) {
     return mad_lo(hi, 16u, lo) - mul_hi(t, 1u << 28) - u;
 }
 
+// Lane l's record to bytes [l * BB, (l + 1) * BB) of the warp's staging, with 32-bit stores
+// (all 32 lanes call it). BB = 2 mod 4 (Q4_0, Q5_0, Q8_0): a lane pair's two records span
+// whole words from the even lane's start; the even lane also writes its partner's first 2
+// bytes (shuffled over), the odd lane the rest of its own record, shifted by 2 bytes.
 template <int BB>
-__device__ __forceinline__ void put_record(uint8_t* o, const uint32_t* rec) {
+__device__ __forceinline__ void put_record(uint8_t* os, int lane, const uint32_t* rec) {
     if constexpr (BB % 4 == 0) {
 #pragma unroll
-        for (int i = 0; i < BB / 4; i++) reinterpret_cast<uint32_t*>(o)[i] = rec[i];
+        for (int i = 0; i < BB / 4; i++) reinterpret_cast<uint32_t*>(os + lane * BB)[i] = rec[i];
     } else {
+        constexpr int H = (BB - 2) / 4;  // whole words before a record's last 2 bytes
+        const uint32_t first = __shfl_down_sync(0xffffffffu, rec[0], 1);
+        uint32_t* w = reinterpret_cast<uint32_t*>(os + (lane & ~1) * BB);  // the pair's first word
+        if ((lane & 1) == 0) {
 #pragma unroll
-        for (int i = 0; i < BB / 2; i++) reinterpret_cast<uint16_t*>(o)[i] = (uint16_t)(rec[i >> 1] >> (16 * (i & 1)));
+            for (int i = 0; i < H; i++) w[i] = rec[i];
+            w[H] = (rec[H] & 0xFFFFu) | (first << 16);
+        } else {
+#pragma unroll
+            for (int i = 0; i < H; i++) w[H + 1 + i] = __funnelshift_r(rec[i], rec[i + 1], 16);
+        }
     }
 }
 
@@ -274,16 +295,14 @@ __device__ __forceinline__ uint32_t high_bits(const uint32_t* W) {
     return h;
 }
 
-// Quantize the block of stage row R into the record at `o`.
+// Quantize the block of stage row R into the record words rec (BB bytes, little-endian).
 template <int QT, int SRC>
-__device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint8_t* o) {
-    constexpr int BB = B32<QT>::BB;
+__device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint32_t* rec) {
     Blk<SRC> B;
     load_block<SRC>(stage, R, B);
     float mx, mn;
     max_min<SRC>(B, mx, mn);
     uint32_t W[8];  // level bytes, 4 per word, block order
-    uint32_t rec[9];
     if constexpr (QT == QS_Q4_0 || QT == QS_Q5_0) {
         // kernels/q4_0.py:20-28: d = max / -8 (max * -0.125, the same value), id = 1 / d,
         // q = clamp(floor(x * id + 8.5), 0, 15). Q5_0: d = max / -16, q = clip(trunc(x * id
@@ -383,21 +402,21 @@ __device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint
         for (int i = 1; i < 8; i++) rec[i] = (W[i - 1] >> 16) | (W[i] << 16);
         rec[8] = W[7] >> 16;
     }
-    put_record<BB>(o, rec);
 }
 
-// Blocks [base, base + a.nblk) of the tensor in one launch (the tensor map starts at `base`).
-template <int QT, int SRC>
-__global__ void __launch_bounds__(B32_THREADS, B32Cfg<QT, es_of<SRC>()>::MIN_CTAS)
+// Blocks [base, base + a.nblk) of the tensor in one launch (the tensor map starts at `base`),
+// in stages of G x 32 blocks.
+template <int QT, int SRC, int G>
+__global__ void __launch_bounds__(B32_THREADS, B32Cfg<QT, es_of<SRC>(), G>::MIN_CTAS)
     blk32_kernel(const __grid_constant__ CUtensorMap map, QuantArgs a, int64_t base) {
     constexpr int ES = es_of<SRC>();
-    using C = B32Cfg<QT, ES>;
-    constexpr int BB = B32<QT>::BB, NST = C::NST, STAGE = C::STAGE;
+    using C = B32Cfg<QT, ES, G>;
+    constexpr int BB = B32<QT>::BB, NSLOT = C::NSLOT, STAGE = C::STAGE, ROWS = C::ROWS;
     extern __shared__ __align__(1024) uint8_t b32_smem_raw[];
     uint8_t* ring = b32_smem_raw;
-    uint8_t* wstage = ring + NST * STAGE;                                       // [CW][2][WST]
-    uint64_t* full = reinterpret_cast<uint64_t*>(wstage + 2 * B32_CW * C::WST);  // [NST]
-    uint64_t* empty = full + NST;                                                // [NST]
+    uint8_t* wstage = ring + NSLOT * STAGE;                                      // [CW][2][WST]
+    uint64_t* full = reinterpret_cast<uint64_t*>(wstage + 2 * B32_CW * C::WST);  // [NSLOT]
+    uint64_t* empty = full + NSLOT;                                              // [NSLOT]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // the swizzle arithmetic needs 1024-byte aligned stages
     if (smem_u32(ring) & 1023) {
@@ -409,47 +428,58 @@ __global__ void __launch_bounds__(B32_THREADS, B32Cfg<QT, es_of<SRC>()>::MIN_CTA
     const int64_t ngroups = (a.nblk + 7) / 8;
     const int64_t g0 = (int64_t)blockIdx.x * ngroups / gridDim.x, g1 = (int64_t)(blockIdx.x + 1) * ngroups / gridDim.x;
     const int64_t b_begin = 8 * g0, b_end = min(8 * g1, a.nblk);
-    const int nstage = (int)((b_end - b_begin + B32_BPS - 1) / B32_BPS);
+    const int nstage = (int)((b_end - b_begin + ROWS - 1) / ROWS);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NST; s++) {
+        for (int s = 0; s < NSLOT; s++) {
             mbar_init(smem_u32(&full[s]), 1);
-            mbar_init(smem_u32(&empty[s]), B32_CW);
+            mbar_init(smem_u32(&empty[s]), G);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        // the next launch on the stream may start its CTAs (they take SM room only as this
+        // grid's CTAs leave, and wait for its completion before reading their inputs)
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     }
     __syncthreads();
 
     if (warp == B32_CW) {  // producer
         if (lane != 0) return;
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map)) : "memory");
+        // under programmatic launch, the previous grid on the stream (which may write this
+        // launch's source, or its destination) completes and its writes become visible here;
+        // the consumers read nothing global and write only after a stage arrives, so the
+        // producer's wait orders the whole CTA (a no-op for an ordinary launch)
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int j = 0; j < nstage; j++) {
-            const int slot = j % NST;
-            if (j >= NST && !mbar_wait(smem_u32(&empty[slot]), (uint32_t)(j / NST - 1) & 1u)) {
+            const int slot = j % NSLOT;
+            if (j >= NSLOT && !mbar_wait(smem_u32(&empty[slot]), (uint32_t)(j / NSLOT - 1) & 1u)) {
                 atomicOr(&g_qs_fault_bits, 1u);
                 return;
             }
-            tensor_load(smem_u32(ring + slot * STAGE), &map, (int)(b_begin + (int64_t)j * B32_BPS), STAGE,
+            tensor_load(smem_u32(ring + slot * STAGE), &map, (int)(b_begin + (int64_t)j * ROWS), STAGE,
                         smem_u32(&full[slot]));
         }
         return;
     }
 
-    // consumers: lane l of warp w quantizes stage row w * 32 + l
+    // consumers: G = 8, every stage, warp w taking rows 32 w .. 32 w + 31; G = 1, stages
+    // w, w + 8, ...; lane l quantizes the warp's row l
     const bool contiguous = a.dst_row_bytes == a.row_bytes;
-    const int R = warp * 32 + lane;
+    const int R = (G == 1 ? 0 : warp * 32) + lane;
     uint8_t* mystage = wstage + warp * 2 * C::WST;
-    for (int i = 0; i < nstage; i++) {
-        const int slot = i % NST;
-        const int64_t b0 = b_begin + (int64_t)i * B32_BPS + warp * 32;
+    for (int i = G == 1 ? warp : 0, k = 0; i < nstage; i += G == 1 ? B32_CW : 1, k++) {
+        const int slot = i % NSLOT;
+        const int64_t b0 = b_begin + (int64_t)i * ROWS + (G == 1 ? 0 : warp * 32);
         const int nb = (int)max((int64_t)0, min((int64_t)32, b_end - b0));
         __syncwarp();  // every lane is done with the staging written two stages ago
-        if (!mbar_wait(smem_u32(&full[slot]), (uint32_t)(i / NST) & 1u)) {
+        if (!mbar_wait(smem_u32(&full[slot]), (uint32_t)(i / NSLOT) & 1u)) {
             if (lane == 0) atomicOr(&g_qs_fault_bits, 1u);
             return;
         }
-        uint8_t* os = mystage + (i & 1) * C::WST;
-        if (lane < nb) quantize_block<QT, SRC>(ring + slot * STAGE, R, os + lane * BB);
+        uint8_t* os = mystage + (k & 1) * C::WST;
+        uint32_t rec[(BB + 3) / 4];
+        if (lane < nb) quantize_block<QT, SRC>(ring + slot * STAGE, R, rec);
+        put_record<BB>(os, lane, rec);  // the whole warp: paired lanes share words
         __syncwarp();  // the warp's reads of the slot and writes of the staging are done
         if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
         uint8_t* d = a.dst + (base + b0) * BB;
@@ -485,13 +515,47 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
+template <int QT, int SRC, int G>
+cudaError_t launch_g(const QuantArgs& p, int64_t base, int grid, const LaunchCtx& ctx) {
+    constexpr int ES = es_of<SRC>();
+    using C = B32Cfg<QT, ES, G>;
+    EncodeTiledFn encode = encode_tiled();
+    if (!encode) return cudaErrorNotSupported;
+    auto k = blk32_kernel<QT, SRC, G>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
+    if (e != cudaSuccess) return e;
+    // the piece's blocks as a (p.nblk rows) x (32 values) tensor, one stage = ROWS rows
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {32, (cuuint64_t)p.nblk};
+    const cuuint64_t strides[1] = {32 * ES};
+    const cuuint32_t box[2] = {32, (cuuint32_t)C::ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    void* gaddr = const_cast<uint8_t*>(static_cast<const uint8_t*>(p.src) + base * 32 * ES);
+    if (encode(&map, ES == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, gaddr, dims, strides,
+               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, ES == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    // programmatic stream serialization: this launch's prologue (barrier set-up, tensor-map
+    // prefetch) overlaps the tail of the previous kernel on the stream
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(B32_THREADS);
+    cfg.dynamicSmemBytes = C::BYTES;
+    cfg.stream = ctx.stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, k, map, p, base);
+}
+
 template <int QT, int SRC>
 cudaError_t launch_t(const QuantArgs& a, const LaunchCtx& ctx) {
     constexpr int ES = es_of<SRC>();
-    using C = B32Cfg<QT, ES>;
-    EncodeTiledFn encode = encode_tiled();
-    if (!encode) return cudaErrorNotSupported;
-    auto k = blk32_kernel<QT, SRC>;
+    using C = B32Cfg<QT, ES, 8>;
+    static_assert(B32Cfg<QT, ES, 1>::BYTES <= C::BYTES + 1024, "both stage shapes fit the same CTAs per SM");
+    auto k = blk32_kernel<QT, SRC, 8>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
@@ -500,25 +564,15 @@ cudaError_t launch_t(const QuantArgs& a, const LaunchCtx& ctx) {
     for (int64_t base = 0; base < a.nblk; base += B32_PIECE) {
         QuantArgs p = a;
         p.nblk = min(B32_PIECE, a.nblk - base);
-        // the piece's blocks as a (p.nblk rows) x (32 values) tensor, one stage = 256 rows
-        CUtensorMap map;
-        const cuuint64_t dims[2] = {32, (cuuint64_t)p.nblk};
-        const cuuint64_t strides[1] = {32 * ES};
-        const cuuint32_t box[2] = {32, B32_BPS};
-        const cuuint32_t estr[2] = {1, 1};
-        void* gaddr = const_cast<uint8_t*>(static_cast<const uint8_t*>(a.src) + base * 32 * ES);
-        if (encode(&map, ES == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, gaddr, dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, ES == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-        const int64_t want = (p.nblk + B32_BPS - 1) / B32_BPS;  // at least one stage per CTA
+        const int64_t want = (p.nblk + C::ROWS - 1) / C::ROWS;  // at least one large stage per CTA
         const int grid = (int)min((int64_t)per_sm * ctx.num_sms, max(want, (int64_t)1));
-        k<<<grid, B32_THREADS, C::BYTES, ctx.stream>>>(map, p, base);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        // fewer than 8 large stages per CTA: the small stages
+        e = p.nblk < (int64_t)grid * 8 * C::ROWS ? launch_g<QT, SRC, 1>(p, base, grid, ctx)
+                                                  : launch_g<QT, SRC, 8>(p, base, grid, ctx);
+        if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
-
 template <int QT>
 cudaError_t launch_q(const QuantArgs& a, const LaunchCtx& ctx) {
     switch (a.src_type) {
