@@ -229,33 +229,6 @@ __device__ __forceinline__ void first_max_min(float& mx, float& mn, const Blk<SR
     mn = b;
 }
 
-// --- packed f32x2 arithmetic (sm_100): two floats in one 64-bit register pair ---------------
-typedef unsigned long long f32x2;
-__device__ __forceinline__ f32x2 f2_pack(float lo, float hi) {
-    f32x2 r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ f32x2 f2_splat(float v) { return f2_pack(v, v); }
-__device__ __forceinline__ void f2_unpack_bits(f32x2 v, uint32_t& lo, uint32_t& hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-}
-__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
-    f32x2 d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
-    f32x2 d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ f32x2 f2_add_rm(f32x2 a, f32x2 b) {  // rounding toward -infinity
-    f32x2 d;
-    asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-
 // --- packing on the FMA pipe ----------------------------------------------------------------
 // The level bytes come out of floor_bits as 0x4B000000 + n (n < 256). Multiplying by 2^8,
 // 2^16 or 2^24 modulo 2^32 drops the 0x4B000000 term, so four levels pack into one word with
@@ -346,17 +319,15 @@ __device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint
         uint32_t qs[4];
         if (!isinf(id)) {
             // x * id, + off and the floor add, two values per packed f32x2 instruction (one
-            // rounding each, as the scalar ones). The product is a fused multiply-add with a +0
-            // addend: the same correctly rounded product (a -0 product becomes +0, which the
-            // + off that follows cannot tell apart), kept apart from the add that follows: a
-            // packed multiply feeding a packed add came out fused into one rounding on sm_100a
+            // rounding each, as the scalar ones; the product as f2_mul_z, whose +0 for a -0
+            // product the + off cannot tell apart)
             const f32x2 id2 = f2_splat(id), off2 = f2_splat(off), big2 = f2_splat(8388608.0f);
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 uint32_t fb[4];
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                    const f32x2 y = f2_fma(f2_pack(B.at(4 * k + 2 * h), B.at(4 * k + 2 * h + 1)), id2, 0ull);
+                    const f32x2 y = f2_mul_z(f2_pack(B.at(4 * k + 2 * h), B.at(4 * k + 2 * h + 1)), id2);
                     f2_unpack_bits(f2_add_rm(f2_add(y, off2), big2), fb[2 * h], fb[2 * h + 1]);
                 }
                 W[k] = pack_levels(fb[0], fb[1], fb[2], fb[3]);

@@ -216,6 +216,72 @@ __device__ __forceinline__ void store_bytes(uint8_t* __restrict__ dst, const uin
     for (int i = head + 16 * body + tid; i < nbytes; i += nthreads) dst[i] = src[i];
 }
 
+// ---------------------------------------------------------------------------
+// packed f32x2 arithmetic (sm_100): two floats in one 64-bit register pair, one rounding
+// per lane as the scalar instruction. ptxas fuses a packed product into a packed add that
+// uses it (one rounding instead of two) even with .rn, and treats a fused multiply-add with
+// a -0 addend as that product; a +0 addend is kept apart, and gives the correctly rounded
+// product except that a -0 product comes out +0. So f2_mul_z is exact wherever the sign of
+// a zero product cannot reach a result; sites where it can keep scalar products (which
+// ptxas does not fuse into packed adds).
+// ---------------------------------------------------------------------------
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 f2_pack(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ f32x2 f2_splat(float v) { return f2_pack(v, v); }
+__device__ __forceinline__ void f2_unpack(f32x2 v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ f32x2 f2_mul_z(f32x2 a, f32x2 b) {  // a * b as fma(a, b, +0): -0 -> +0
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(0ull));
+    return d;
+}
+__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f32x2 f2_sub(f32x2 a, f32x2 b) {
+    f32x2 d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ f32x2 f2_abs(f32x2 a) { return a & 0x7FFFFFFF7FFFFFFFull; }
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f32x2 f2_add_rm(f32x2 a, f32x2 b) {  // rounding toward -infinity
+    f32x2 d;
+    asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ void f2_unpack_bits(f32x2 v, uint32_t& lo, uint32_t& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+}
+
+// The adjacent-pair tree of 2H values held as pairs (v[k], v[k + H]): both halves' trees
+// run side by side, and the last level adds them, as the scalar tree does.
+template <int H>
+__device__ __forceinline__ float tree_sum2(const f32x2* t) {
+    f32x2 a[H];
+#pragma unroll
+    for (int i = 0; i < H; i++) a[i] = t[i];
+#pragma unroll
+    for (int n = H; n > 1; n >>= 1) {
+#pragma unroll
+        for (int i = 0; i < n / 2; i++) a[i] = f2_add(a[2 * i], a[2 * i + 1]);
+    }
+    float lo, hi;
+    f2_unpack(a[0], lo, hi);
+    return __fadd_rn(lo, hi);
+}
+
 // Parameters shared by every quantize launch.
 struct QuantArgs {
     const void* src;      // n_rows x k elements of src_type, row-major, contiguous

@@ -473,31 +473,8 @@ __device__ __forceinline__ bool cert_ok(const IqCertSub& c, float sc, float apma
     return sc >= 0x1p-40f && sc <= 0x1p16f && c.S0 <= 0x1p40f && c.XM <= 0x1p40f && Q >= 0x1p-40f && Q <= 0x1p60f;
 }
 
-// Two floats in one 64-bit register pair for the packed f32x2 arithmetic of sm_100 (one
-// rounding per lane, as the scalar instruction). The certified pass is free to use it: its
-// bound counts one rounding per operation and term, whatever the order.
-typedef unsigned long long f32x2;
-__device__ __forceinline__ f32x2 f2_pack(float lo, float hi) {
-    f32x2 r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(f32x2 v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
-__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
-    f32x2 d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
-    f32x2 d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
-    f32x2 d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
+// The certified pass uses the packed f32x2 arithmetic of qs_common.cuh: its bound counts one
+// rounding per operation and term, whatever the order.
 
 // A' and L of one candidate from its level bytes (one per position), two positions per
 // packed operation; ws2 / sx2 hold s and s x of positions 2k, 2k + 1.
@@ -513,8 +490,8 @@ __device__ __forceinline__ void cert_terms(const uint32_t* lw, const f32x2* ws2,
                                         __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7440u | ((2 * k + 1) & 3)))),
                                 M223);
         const f32x2 p = f2_fma(lf, lf, lf);
-        a2 = k == 0 ? f2_mul(ws2[0], p) : f2_fma(ws2[k], p, a2);
-        b2 = k == 0 ? f2_mul(sx2[0], lf) : f2_fma(sx2[k], lf, b2);
+        a2 = k == 0 ? f2_mul_z(ws2[0], p) : f2_fma(ws2[k], p, a2);
+        b2 = k == 0 ? f2_mul_z(sx2[0], lf) : f2_fma(sx2[k], lf, b2);
     }
     float a0, a1, b0, b1;
     f2_unpack(a2, a0, a1);

@@ -37,40 +37,102 @@ __device__ __forceinline__ float qkx_search(const float* x, const float* w, cons
     // the accepted levels are rebuilt from (isc, mn) of the winning step at the end
     float win_isc = iscale, win_mn = mn;
 
+    if constexpr (N == 32) {
+        // the candidate steps on packed pairs (v[k], v[k + N/2]): every operation is the scalar
+        // one, two values at a time, and the adjacent-pair trees stay lane-parallel (tree_sum2).
+        // Products are f2_mul_z (a -0 product comes out +0) where that sign cannot reach a result:
+        // isc (x - mn) feeds the rounding add; w l and w l l are -0 only for a -0 weight, and
+        // their sums matter only when nonzero (D > 0); the residual products are squared or
+        // taken absolute after + tm - x. w l x keeps scalar products: a zero weight on a negative
+        // value makes a -0 term, and an all-zero sum_xl's sign reaches ts.
+        constexpr int H = N / 2;
+        f32x2 x2[H], w2[H];
+#pragma unroll
+        for (int k = 0; k < H; k++) {
+            x2[k] = f2_pack(x[k], x[k + H]);
+            w2[k] = f2_pack(w[k], w[k + H]);
+        }
+        const f32x2 magic = f2_splat(12582912.0f), nmagic = f2_splat(-12582912.0f);
 #pragma unroll 1
-    for (int s = 0; s < nsteps; s++) {
-        const float isc = __fdiv_rn(steps[s], degen ? 1.0f : mx - mn);
-        float la[N], wl[N], wl2[N], wlx[N];
+        for (int s = 0; s < nsteps; s++) {
+            const float isc = __fdiv_rn(steps[s], degen ? 1.0f : mx - mn);
+            const f32x2 isc2 = f2_splat(isc), mn2 = f2_splat(mn);
+            f32x2 la[H], wl[H], wl2[H], wlx[H];
 #pragma unroll
-        for (int i = 0; i < N; i++) {
-            la[i] = clamp_nan(rint_add(isc * (x[i] - mn)), 0.0f, fmax);
-            wl[i] = w[i] * la[i];
-            wl2[i] = wl[i] * la[i];
-            wlx[i] = wl[i] * x[i];
-        }
-        const float sum_l = tree_sum<N>(wl);
-        const float sum_l2 = tree_sum<N>(wl2);
-        const float sum_xl = tree_sum<N>(wlx);
-        const float D = sum_w * sum_l2 - sum_l * sum_l;
-        const float Dsafe = D > 0.0f ? D : 1.0f;
-        float ts = __fdiv_rn(sum_w * sum_xl - sum_x * sum_l, Dsafe);
-        float tm = __fdiv_rn(sum_l2 * sum_x - sum_l * sum_xl, Dsafe);
-        if (tm > 0.0f) {
-            ts = __fdiv_rn(sum_xl, sum_l2 < F32_TINY ? F32_TINY : sum_l2);
-            tm = 0.0f;
-        }
+            for (int k = 0; k < H; k++) {
+                // clamp(rint_add(isc * (x - mn)), 0, fmax), the clamp per lane
+                float l0, l1;
+                f2_unpack(f2_add(f2_add(f2_mul_z(isc2, f2_sub(x2[k], mn2)), magic), nmagic), l0, l1);
+                la[k] = f2_pack(clamp_nan(l0, 0.0f, fmax), clamp_nan(l1, 0.0f, fmax));
+                wl[k] = f2_mul_z(w2[k], la[k]);
+                wl2[k] = f2_mul_z(wl[k], la[k]);
+                float a0, a1;
+                f2_unpack(wl[k], a0, a1);
+                wlx[k] = f2_pack(a0 * x[k], a1 * x[k + H]);
+            }
+            const float sum_l = tree_sum2<H>(wl);
+            const float sum_l2 = tree_sum2<H>(wl2);
+            const float sum_xl = tree_sum2<H>(wlx);
+            const float D = sum_w * sum_l2 - sum_l * sum_l;
+            const float Dsafe = D > 0.0f ? D : 1.0f;
+            float ts = __fdiv_rn(sum_w * sum_xl - sum_x * sum_l, Dsafe);
+            float tm = __fdiv_rn(sum_l2 * sum_x - sum_l * sum_xl, Dsafe);
+            if (tm > 0.0f) {
+                ts = __fdiv_rn(sum_xl, sum_l2 < F32_TINY ? F32_TINY : sum_l2);
+                tm = 0.0f;
+            }
+            const f32x2 ts2 = f2_splat(ts), tm2 = f2_splat(tm);
+            f32x2 t2[H];
 #pragma unroll
-        for (int i = 0; i < N; i++) {
-            float d = (ts * la[i] + tm) - x[i];
-            t[i] = MAD ? w[i] * fabsf(d) : w[i] * (d * d);
+            for (int k = 0; k < H; k++) {
+                const f32x2 d = f2_sub(f2_add(f2_mul_z(ts2, la[k]), tm2), x2[k]);  // (ts * la + tm) - x
+                t2[k] = MAD ? f2_mul_z(w2[k], f2_abs(d)) : f2_mul_z(w2[k], f2_mul_z(d, d));
+            }
+            const float cur = tree_sum2<H>(t2);
+            if (D > 0.0f && cur < best && !degen) {
+                win_isc = isc;
+                win_mn = mn;
+                scale = ts;
+                mn = tm;
+                best = cur;
+            }
         }
-        const float cur = tree_sum<N>(t);
-        if (D > 0.0f && cur < best && !degen) {
-            win_isc = isc;
-            win_mn = mn;
-            scale = ts;
-            mn = tm;
-            best = cur;
+    } else {  // 16-value groups: scalar (the packed form measured 6 % slower on Q2_K)
+#pragma unroll 1
+        for (int s = 0; s < nsteps; s++) {
+            const float isc = __fdiv_rn(steps[s], degen ? 1.0f : mx - mn);
+            float la[N], wl[N], wl2[N], wlx[N];
+#pragma unroll
+            for (int i = 0; i < N; i++) {
+                la[i] = clamp_nan(rint_add(isc * (x[i] - mn)), 0.0f, fmax);
+                wl[i] = w[i] * la[i];
+                wl2[i] = wl[i] * la[i];
+                wlx[i] = wl[i] * x[i];
+            }
+            const float sum_l = tree_sum<N>(wl);
+            const float sum_l2 = tree_sum<N>(wl2);
+            const float sum_xl = tree_sum<N>(wlx);
+            const float D = sum_w * sum_l2 - sum_l * sum_l;
+            const float Dsafe = D > 0.0f ? D : 1.0f;
+            float ts = __fdiv_rn(sum_w * sum_xl - sum_x * sum_l, Dsafe);
+            float tm = __fdiv_rn(sum_l2 * sum_x - sum_l * sum_xl, Dsafe);
+            if (tm > 0.0f) {
+                ts = __fdiv_rn(sum_xl, sum_l2 < F32_TINY ? F32_TINY : sum_l2);
+                tm = 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < N; i++) {
+                float d = (ts * la[i] + tm) - x[i];
+                t[i] = MAD ? w[i] * fabsf(d) : w[i] * (d * d);
+            }
+            const float cur = tree_sum<N>(t);
+            if (D > 0.0f && cur < best && !degen) {
+                win_isc = isc;
+                win_mn = mn;
+                scale = ts;
+                mn = tm;
+                best = cur;
+            }
         }
     }
 #pragma unroll
