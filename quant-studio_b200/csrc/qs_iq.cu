@@ -311,7 +311,8 @@ struct IqWarpSmem {
                                      // holds the superblock squares while the weights are computed
     __align__(16) float wv[32][XS];  // sqrt of the weights
     float rg[32];                    // per group: r, the search scale of step j being 1 / (r c_j)
-    float psc[32][Tr::SW <= 8 ? Tr::SW : 1];  // short windows: those scales, per group and step
+    float psc[32][Tr::SW <= 8 ? Tr::SW + 1 : 1];  // short windows: those scales (odd pitch: random groups
+                                                  // read by the lanes spread over the banks)
     float fsc[32];                   // per group: the scale of the final reprojection
     unsigned long long xflag[32];    // per group: steps (bit j * NSUB + q) left to an exact search
     uint32_t rec[IQ_CAP];            // queue: the code's nbr entry (list start and length)

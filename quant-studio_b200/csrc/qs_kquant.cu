@@ -298,40 +298,41 @@ __global__ void __launch_bounds__(256) qx_kernel(QuantArgs a, KParams p) {
         *reinterpret_cast<uint4*>(lev + g * GS) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         __syncwarp();
 
+        // packing: a lane's output bytes come from runs of 4 or 8 consecutive level bytes, read
+        // as words and combined four bytes at a time (no byte-wide shared-memory traffic)
         uint8_t* o = s_out + sbl * BB;
+        auto put32 = [&](int off, uint32_t v) {  // o + off is 2-byte aligned (BB is even)
+            reinterpret_cast<uint16_t*>(o + off)[0] = (uint16_t)v;
+            reinterpret_cast<uint16_t*>(o + off)[1] = (uint16_t)(v >> 16);
+        };
+        auto lw = [&](int off) { return *reinterpret_cast<const uint32_t*>(lev + off); };
         if (T == QS_Q6_K) {
-#pragma unroll
-            for (int i = 8 * g; i < 8 * g + 8; i++) {  // ql
-                const int h = i >> 6, r = i & 63, l = r & 31, hi = r >> 5;
-                const uint8_t* q = lev + 128 * h + 32 * hi + l;
-                o[i] = (uint8_t)((q[0] & 0xF) | ((q[64] & 0xF) << 4));
+            {  // ql bytes 8g..8g+7: low nibbles of levels [A, A + 8) and [A + 64, A + 72)
+                const int A = 128 * (g >> 3) + 32 * ((g >> 2) & 1) + 8 * (g & 3);
+                const uint2 q0 = *reinterpret_cast<const uint2*>(lev + A), q1 = *reinterpret_cast<const uint2*>(lev + A + 64);
+                put32(8 * g, (q0.x & 0x0F0F0F0Fu) | ((q1.x & 0x0F0F0F0Fu) << 4));
+                put32(8 * g + 4, (q0.y & 0x0F0F0F0Fu) | ((q1.y & 0x0F0F0F0Fu) << 4));
             }
-#pragma unroll
-            for (int i = 4 * g; i < 4 * g + 4; i++) {  // qh
-                const int h = i >> 5, l = i & 31;
-                const uint8_t* q = lev + 128 * h + l;
-                o[128 + i] = (uint8_t)((q[0] >> 4) | ((q[32] >> 4) << 2) | ((q[64] >> 4) << 4) | ((q[96] >> 4) << 6));
+            {  // qh bytes 4g..4g+3: bits 4-5 of levels C, C + 32, C + 64, C + 96 (+ 0..3)
+                const int C = 128 * (g >> 3) + 4 * (g & 7);
+                put32(128 + 4 * g, ((lw(C) >> 4) & 0x03030303u) | (((lw(C + 32) >> 4) & 0x03030303u) << 2) |
+                                       (((lw(C + 64) >> 4) & 0x03030303u) << 4) | (((lw(C + 96) >> 4) & 0x03030303u) << 6));
             }
             o[192 + g] = (uint8_t)(int8_t)myls;
             if (g == 0) { o[208] = (uint8_t)d16; o[209] = (uint8_t)(d16 >> 8); }
         } else {
+            {  // hmask bytes 2g, 2g + 1: bit bb = level[32 bb + l] > 3 (its bit 2), for the four l of
+               // one word, of which this lane keeps two
+                const int W = 4 * (g >> 1);
+                uint32_t acc = 0;
 #pragma unroll
-            for (int l = 2 * g; l < 2 * g + 2; l++) {  // hmask
-                int v = 0;
-#pragma unroll
-                for (int bb = 0; bb < 8; bb++) v |= (lev[32 * bb + l] > 3) << bb;
-                o[l] = (uint8_t)v;
+                for (int bb = 0; bb < 8; bb++) acc |= ((lw(32 * bb + W) >> 2) & 0x01010101u) << bb;
+                reinterpret_cast<uint16_t*>(o + 2 * g)[0] = (uint16_t)(acc >> (16 * (g & 1)));
             }
-#pragma unroll
-            for (int i = 4 * g; i < 4 * g + 4; i++) {  // qs
-                const int h = i >> 5, l = i & 31;
-                int v = 0;
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    int q = lev[128 * h + 32 * j + l];
-                    v |= (q > 3 ? q - 4 : q) << (2 * j);
-                }
-                o[32 + i] = (uint8_t)v;
+            {  // qs bytes 4g..4g+3: the low 2 bits of levels D + 32 j (j = 0..3; q > 3 ? q - 4 : q)
+                const int D = 128 * (g >> 3) + 4 * (g & 7);
+                put32(32 + 4 * g, (lw(D) & 0x03030303u) | ((lw(D + 32) & 0x03030303u) << 2) |
+                                      ((lw(D + 64) & 0x03030303u) << 4) | ((lw(D + 96) & 0x03030303u) << 6));
             }
             if (g < 8) {
                 const int a0 = (int)s_ls[sbl][g], a8 = (int)s_ls[sbl][g + 8];
