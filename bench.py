@@ -68,7 +68,14 @@ ALG_OPS = {("q4_k", True): 655, ("q4_k", False): 21 * 17 + 11 + 3 + 4 + 7,
            ("iq2_s", True): round(13.3 * 33) + 20 * 12 + 15, ("iq3_xxs", True): round(50.8 * 17) + 32 * 12 + 15,
            ("iq3_s", True): round(38.9 * 17) + 20 * 12 + 15,
            # the 32-value block formats: block max/min, one scale, 3-4 ops per value
-           ("q4_1", False): 10, ("q5_0", False): 10, ("q5_1", False): 10, ("q8_0", False): 8}
+           ("q4_1", False): 10, ("q5_0", False): 10, ("q5_1", False): 10, ("q8_0", False): 8,
+           # Q3_K: with imatrix the make_qx search of Q6_K (nmax 4); without, make_q3_quants: the
+           # initial fit (9 per value), 5 greedy passes x 19 (both sums' updates, the division,
+           # round, clamps, the comparison), the superblock-scale fit and packing (19)
+           ("q3_k", True): 19 * 9 + 18, ("q3_k", False): 9 + 5 * 19 + 19,
+           # IQ4_XS: 16 candidate scales x 14 (id x, the 4-step bracket and midpoint compare of
+           # the non-linear grid, two weighted products and sums) + 18 (weights, requantize, pack)
+           ("iq4_xs", True): 16 * 14 + 18, ("iq4_xs", False): 16 * 14 + 18}
 ALG_BYTES_OUT = {"q4_0": 18 / 32, "q2_k": 84 / 256, "q3_k": 110 / 256, "q4_k": 144 / 256,
                  "q5_k": 176 / 256, "q6_k": 210 / 256, "iq4_xs": 136 / 256, "iq2_xxs": 66 / 256,
                  "iq2_xs": 74 / 256, "iq2_s": 82 / 256, "iq3_xxs": 98 / 256, "iq3_s": 110 / 256,
