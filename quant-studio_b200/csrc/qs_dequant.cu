@@ -327,6 +327,10 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
     __shared__ double s_red[2][DQ_THREADS / 32];
     const int tid = threadIdx.x, lb = tid / TPB, t = tid % TPB;
     const bool packed = a.src_row_bytes == a.nblk_row * D::BB;
+    // the error passes read packed blocks straight from global memory (L1): they also load
+    // the source rows, and staging the blocks cost two CTA barriers a tile (their main stall,
+    // +7-9 % without); decode keeps the coalesced 16-byte staging (5-12 % faster there)
+    const bool direct = MODE != DQ_DECODE && packed;
     double acc_w = 0.0, acc = 0.0;
 
     // Packed rows: a tile is one contiguous span of nb * BB bytes, at most one 16-byte body
@@ -353,7 +357,7 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
         if (ti < sh.nbytes) sh.tl = __ldg(g + ti);
     };
     Share cur;
-    if (packed && (int64_t)blockIdx.x * BPT < a.nblk) fetch(blockIdx.x, cur);
+    if (packed && !direct && (int64_t)blockIdx.x * BPT < a.nblk) fetch(blockIdx.x, cur);
 
     for (int64_t tile = blockIdx.x; tile * BPT < a.nblk; tile += gridDim.x) {
         const int64_t b0 = tile * BPT;
@@ -368,7 +372,9 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
             if (a.qw) load_f32<8>(a.qw + col, cw);
         }
         const uint8_t* tb;
-        if (packed) {
+        if (direct) {
+            tb = a.src + b0 * D::BB;
+        } else if (packed) {
             uint8_t* sp = s_blk + cur.mis;
             if (tid < cur.body) reinterpret_cast<uint4*>(sp + cur.head)[tid] = cur.v;
             if (tid < cur.head) sp[tid] = cur.h;
@@ -383,9 +389,11 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
             }
             tb = s_blk;
         }
-        __syncthreads();
-        if (packed && (tile + gridDim.x) * BPT < a.nblk) fetch(tile + gridDim.x, cur);  // the next tile
-        __syncthreads();
+        if (!direct) {
+            __syncthreads();
+            if (packed && (tile + gridDim.x) * BPT < a.nblk) fetch(tile + gridDim.x, cur);  // the next tile
+            __syncthreads();
+        }
         if (live) {
             float v[8];
             D::decode(tb + lb * D::BB, t, a.kgrid, v);
@@ -419,7 +427,7 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
                 }
             }
         }
-        __syncthreads();
+        if (!direct) __syncthreads();
     }
     if (MODE == DQ_SUM_ERR) {
         // CTA partial: xor tree within each warp, then warps in order
