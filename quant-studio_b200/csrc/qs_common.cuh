@@ -69,7 +69,8 @@ __device__ __forceinline__ void load_f32(const float* p, float* v) {
 // ---------------------------------------------------------------------------
 // exact scalar helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float rcp_rn(float x) { return __fdiv_rn(1.0f, x); }
+// 1 / x correctly rounded (the reciprocal intrinsic: the same value as the IEEE division 1 / x)
+__device__ __forceinline__ float rcp_rn(float x) { return __frcp_rn(x); }
 __device__ __forceinline__ float clampf(float x, float lo, float hi) { return x < lo ? lo : (x > hi ? hi : x); }
 __device__ __forceinline__ float min_hi(float x, float hi) { return x > hi ? hi : x; }
 // clampf for the search loops, two NaN-propagating min/max instructions: equal to clampf for
