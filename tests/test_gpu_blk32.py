@@ -113,3 +113,21 @@ def test_no_kernel_gave_up_waiting():
     bits = ctypes.c_int(-1)
     _native.check(_native.lib().qs_device_fault(0, ctypes.byref(bits)))
     assert bits.value == 0
+
+
+@pytest.mark.parametrize("qtype", list(TYPES))
+def test_launch_waits_for_the_kernel_that_wrote_its_input(qtype):
+    """Each launch may start while the previous kernel on its stream finishes (programmatic
+    stream serialization); it must still read the rows that kernel wrote, and its blocks must
+    land after those of an earlier launch into the same destination."""
+    s = torch.cuda.Stream()
+    base = torch.from_numpy(bench_rows(4096, 4096, 21)).to(torch.bfloat16).cuda()
+    rb = _native.row_bytes(int(TYPES[qtype]), 4096)
+    out = torch.empty((4096, rb), dtype=torch.uint8, device="cuda")
+    with torch.cuda.stream(s):
+        for scale in (0.5, 3.0, -1.25):
+            y = base * scale  # a torch kernel on the same stream writes the source rows
+            _native.quantize_into(int(TYPES[qtype]), y, None, out, s)
+    s.synchronize()
+    want = oracle.quantize(qtype, (base.float() * -1.25).to(torch.bfloat16).float().cpu().numpy())
+    assert np.array_equal(out.cpu().numpy(), want)
