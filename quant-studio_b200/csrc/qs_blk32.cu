@@ -230,12 +230,10 @@ __device__ __forceinline__ void first_max_min(float& mx, float& mn, const Blk<SR
 }
 
 // --- packing on the FMA pipe ----------------------------------------------------------------
-// The level bytes come out of floor_bits as 0x4B000000 + n (n < 256). Multiplying by 2^8,
-// 2^16 or 2^24 modulo 2^32 drops the 0x4B000000 term, so four levels pack into one word with
-// integer multiply-adds (IMAD, FMA pipe) instead of byte permutes on the ALU pipe.
 // floor(v) for v in [0, 2^23): v + 2^23 added rounding toward -infinity is the float
-// 2^23 + floor(v), whose bits are 0x4B000000 + floor(v).
-__device__ __forceinline__ uint32_t floor_bits(float v) { return (uint32_t)__float_as_int(__fadd_rd(v, 8388608.0f)); }
+// 2^23 + floor(v), whose bits are 0x4B000000 + floor(v) (the "floor bits" of v). Multiplying
+// those by 2^8, 2^16 or 2^24 modulo 2^32 drops the 0x4B000000 term, so four levels pack into
+// one word with integer multiply-adds (IMAD, FMA pipe) instead of byte permutes on the ALU pipe.
 __device__ __forceinline__ uint32_t mad_lo(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t r;
     asm("mad.lo.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
@@ -246,7 +244,7 @@ __device__ __forceinline__ uint32_t mul_hi(uint32_t a, uint32_t b) {
     asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
 }
-// bytes n0 | n1 << 8 | n2 << 16 | n3 << 24 from four floor_bits results
+// bytes n0 | n1 << 8 | n2 << 16 | n3 << 24 from the floor bits of four levels
 __device__ __forceinline__ uint32_t pack_levels(uint32_t f0, uint32_t f1, uint32_t f2, uint32_t f3) {
     return mad_lo(f3, 1u << 24, mad_lo(f2, 1u << 16, mad_lo(f1, 1u << 8, f0 - 0x4B000000u)));
 }
@@ -376,10 +374,19 @@ __device__ __forceinline__ void quantize_block(const uint8_t* stage, int R, uint
         const float d = __fdiv_rn(mx - mn, QT == QS_Q4_1 ? 15.0f : 31.0f);
         float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
         id = isinf(id) ? 0.0f : id;
+        // x - mn, * id, + 0.5 and the floor add on packed f32x2, two values per instruction
+        // (x - mn >= +0 and id >= 0: the +0-addend product is the exact product here)
+        const f32x2 mn2 = f2_splat(mn), id2 = f2_splat(id), half2 = f2_splat(0.5f), big2 = f2_splat(8388608.0f);
 #pragma unroll
-        for (int k = 0; k < 8; k++)
-            W[k] = pack_levels(floor_bits((B.at(4 * k) - mn) * id + 0.5f), floor_bits((B.at(4 * k + 1) - mn) * id + 0.5f),
-                               floor_bits((B.at(4 * k + 2) - mn) * id + 0.5f), floor_bits((B.at(4 * k + 3) - mn) * id + 0.5f));
+        for (int k = 0; k < 8; k++) {
+            uint32_t fb[4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const f32x2 y = f2_mul_z(f2_sub(f2_pack(B.at(4 * k + 2 * h), B.at(4 * k + 2 * h + 1)), mn2), id2);
+                f2_unpack_bits(f2_add_rm(f2_add(y, half2), big2), fb[2 * h], fb[2 * h + 1]);
+            }
+            W[k] = pack_levels(fb[0], fb[1], fb[2], fb[3]);
+        }
         uint32_t qs[4];
         if constexpr (QT == QS_Q4_1) {
 #pragma unroll
