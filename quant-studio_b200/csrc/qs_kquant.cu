@@ -367,7 +367,62 @@ __device__ __forceinline__ int iq4nl_index(const float* kv, float al) {
     return (al - kv[mu - 1] < kv[mu] - al) ? mu - 1 : mu;
 }
 
-constexpr int IQ4XS_THREADS = 128, IQ4XS_MIN_CTAS = 3;  // 3 CTAs of 4 warps per SM at <= 168 registers
+// The scale search's level lookup without a search. Because the table is integer,
+// kv[j] <= al exactly when kv[j] <= floor(al), so the bracket kv[p] <= al < kv[p + 1] (p
+// clamped to 0..14 as searchsorted + clamp does) is a function of floor(al). A floor in
+// [-136, 134] indexes a table of brackets {kv[p], kv[p + 1]} held as two bf16 halves (the
+// levels are 7-bit integers, exact in bf16). The table keeps one column per lane (word
+// 32 e + lane), so a warp's 32 lookups hit 32 banks whatever the values. The midpoint
+// compare then runs on al itself, in the reference's float arithmetic. Clamping before the
+// floor keeps every value exact: below -136 the bracket is {kv[0], kv[1]} and above 134 it is
+// {kv[14], kv[15]}, as for any al beyond kv[1] or kv[14]. A NaN clamps to -136, fails the
+// compare and takes kv[1], as the search does.
+constexpr int IQ4_TAB_LO = -136, IQ4_TAB_N = 271;                 // floors -136..134
+constexpr float IQ4_TAB_FLOOR = 12582912.0f - (float)IQ4_TAB_LO;  // 1.5 * 2^23 + 136
+constexpr size_t IQ4_TAB_BYTES = (size_t)IQ4_TAB_N * 32 * 4;
+
+__device__ __forceinline__ uint32_t iq4_tab_row(float al) {  // floor(clamp(al)) - IQ4_TAB_LO
+    const float y = fminf(fmaxf(al, (float)IQ4_TAB_LO), 134.5f);
+    // y + 1.5 * 2^23 + 136 lies in [2^23, 2^24), where one ulp is 1: rounding down leaves
+    // floor(y) + 136 in the low mantissa bits
+    return __float_as_uint(__fadd_rd(y, IQ4_TAB_FLOOR)) & 0x1FFu;
+}
+__device__ __forceinline__ float iq4_tab_level(const uint32_t* tab, float al) {
+    const uint32_t w = tab[iq4_tab_row(al) * 32];
+    const float lo = __uint_as_float(w << 16), hi = __uint_as_float(w & 0xFFFF0000u);
+    return (al - lo < hi - al) ? lo : hi;
+}
+__device__ __forceinline__ f32x2 iq4_tab_level2(const uint32_t* tab, f32x2 al) {
+    float a0, a1;
+    f2_unpack(al, a0, a1);
+    uint32_t b0, b1;
+    f2_unpack_bits(f2_add_rm(f2_pack(fminf(fmaxf(a0, (float)IQ4_TAB_LO), 134.5f), fminf(fmaxf(a1, (float)IQ4_TAB_LO), 134.5f)),
+                             f2_splat(IQ4_TAB_FLOOR)),
+                   b0, b1);
+    const uint32_t w0 = tab[(b0 & 0x1FFu) * 32], w1 = tab[(b1 & 0x1FFu) * 32];
+    const f32x2 lo = f2_pack(__uint_as_float(w0 << 16), __uint_as_float(w1 << 16));
+    const f32x2 hi = f2_pack(__uint_as_float(w0 & 0xFFFF0000u), __uint_as_float(w1 & 0xFFFF0000u));
+    float d0, d1, e0, e1, l0, l1, h0, h1;
+    f2_unpack(f2_sub(al, lo), d0, d1);
+    f2_unpack(f2_sub(hi, al), e0, e1);
+    f2_unpack(lo, l0, l1);
+    f2_unpack(hi, h0, h1);
+    return f2_pack(d0 < e0 ? l0 : h0, d1 < e1 ? l1 : h1);
+}
+
+// Fills the lane-column bracket table (IQ4_TAB_N rows of 32 words).
+__device__ __forceinline__ void iq4_tab_fill(uint32_t* tab, int tid, int nthreads) {
+    for (int i = tid; i < IQ4_TAB_N * 32; i += nthreads) {
+        const float f = (float)(i / 32 + IQ4_TAB_LO);
+        int p = 0;
+        for (int j = 1; j <= 14; j++) p += c_kv_iq4nl[j] <= f;
+        tab[i] = (__float_as_uint(c_kv_iq4nl[p]) >> 16) | (__float_as_uint(c_kv_iq4nl[p + 1]) & 0xFFFF0000u);
+    }
+}
+
+// 4 CTAs of 4 warps per SM at <= 128 registers; each CTA holds 19 KB of static shared memory
+// and the 34.7 KB bracket table
+constexpr int IQ4XS_THREADS = 128, IQ4XS_MIN_CTAS = 4;
 
 template <bool IMAT>
 __global__ void __launch_bounds__(IQ4XS_THREADS, IQ4XS_MIN_CTAS) iq4xs_kernel(QuantArgs a) {
@@ -376,10 +431,13 @@ __global__ void __launch_bounds__(IQ4XS_THREADS, IQ4XS_MIN_CTAS) iq4xs_kernel(Qu
     __shared__ __align__(16) float s_sq[SBT * QK_K];
     __shared__ float s_part[SBT][8], s_sc[SBT][NG];
     __shared__ __align__(16) uint8_t s_out[SBT * BB];
+    extern __shared__ uint32_t s_l4[];  // IQ4_TAB_N x 32 lane columns
     const int tid = threadIdx.x, sbl = tid / NG, g = tid % NG;
     if (tid < 16) s_kv[tid] = c_kv_iq4nl[tid];
+    iq4_tab_fill(s_l4, tid, IQ4XS_THREADS);
     __syncthreads();
     float* sq = s_sq + sbl * QK_K;
+    const uint32_t* tab = s_l4 + (tid & 31);
 
     for (int64_t tile = blockIdx.x; tile * SBT < a.nblk; tile += gridDim.x) {
         const int64_t b = min(tile * SBT + sbl, a.nblk - 1);
@@ -412,7 +470,7 @@ __global__ void __launch_bounds__(IQ4XS_THREADS, IQ4XS_MIN_CTAS) iq4xs_kernel(Qu
             float u[GS];
 #pragma unroll
             for (int i = 0; i < GS; i++) {
-                const float q = s_kv[iq4nl_index(s_kv, id0 * x[i])];
+                const float q = iq4_tab_level(tab, id0 * x[i]);
                 t[i] = (w[i] * q) * x[i];
                 u[i] = (w[i] * q) * q;
             }
@@ -422,16 +480,24 @@ __global__ void __launch_bounds__(IQ4XS_THREADS, IQ4XS_MIN_CTAS) iq4xs_kernel(Qu
         float d = sumq2 > 0.0f ? __fdiv_rn(sumqx, sumq2) : 0.0f;
         float best = d * sumqx;
         const float r = rcp_rn(mxs);
+        // Sweep products on f32x2 pairs. The sign of a zero product cannot reach the result:
+        // best >= 0 throughout (sumqx^2 / sumq2 with sumq2 > 0, or a signed zero), so a step
+        // is accepted only with sumqx != 0 and sumq2 > 0, whose values the sign of a zero
+        // term does not change.
 #pragma unroll 1
         for (int itry = -7; itry <= 7; itry++) {
-            const float idv = r * (float)(itry - 127);
+            const f32x2 idv = f2_splat(r * (float)(itry - 127));
             float sx = 0.0f, s2 = 0.0f;
 #pragma unroll
-            for (int i = 0; i < GS; i++) {
-                const float q = s_kv[iq4nl_index(s_kv, idv * x[i])];
-                const float wq = w[i] * q;
-                sx = i == 0 ? wq * x[i] : sx + wq * x[i];
-                s2 = i == 0 ? wq * q : s2 + wq * q;
+            for (int i = 0; i < GS; i += 2) {
+                const f32x2 xx = f2_pack(x[i], x[i + 1]);
+                const f32x2 q = iq4_tab_level2(tab, f2_mul_z(idv, xx));
+                const f32x2 wq = f2_mul_z(f2_pack(w[i], w[i + 1]), q);
+                float tx0, tx1, tq0, tq1;
+                f2_unpack(f2_mul_z(wq, xx), tx0, tx1);
+                f2_unpack(f2_mul_z(wq, q), tq0, tq1);
+                sx = i == 0 ? __fadd_rn(tx0, tx1) : __fadd_rn(__fadd_rn(sx, tx0), tx1);
+                s2 = i == 0 ? __fadd_rn(tq0, tq1) : __fadd_rn(__fadd_rn(s2, tq0), tq1);
             }
             if (s2 > 0.0f && sx * sx > best * s2) {
                 const float nd = __fdiv_rn(sx, s2);
@@ -549,8 +615,10 @@ cudaError_t launch_kquant(int type, const QuantArgs& a, const LaunchCtx& ctx) {
     case QS_IQ4_XS: {
         constexpr int SBT = IQ4XS_THREADS / 8;
         const int64_t tiles = (a.nblk + SBT - 1) / SBT;
-        if (imat) { auto k = iq4xs_kernel<true>; iq4xs_kernel<true><<<grid_for(k, tiles, ctx, 0, IQ4XS_THREADS), IQ4XS_THREADS, 0, st>>>(a); }
-        else { auto k = iq4xs_kernel<false>; iq4xs_kernel<false><<<grid_for(k, tiles, ctx, 0, IQ4XS_THREADS), IQ4XS_THREADS, 0, st>>>(a); }
+        auto k = imat ? iq4xs_kernel<true> : iq4xs_kernel<false>;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)IQ4_TAB_BYTES);
+        if (e != cudaSuccess) return e;
+        k<<<grid_for(k, tiles, ctx, IQ4_TAB_BYTES, IQ4XS_THREADS), IQ4XS_THREADS, IQ4_TAB_BYTES, st>>>(a);
         break;
     }
     default:
