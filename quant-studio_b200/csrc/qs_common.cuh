@@ -177,6 +177,31 @@ __device__ __forceinline__ float sb_sum256_partial(const float* sq, int lane8) {
     }
     return __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
 }
+
+// The same sum for 32-value groups (8 per superblock, group g's values x[0..31] are elements
+// 32 g + c), from a layout without bank conflicts. Partial `lane8` reads the columns
+// c = lane8 + 8 k (k = 0..3) of every group row, so row g keeps those four columns together
+// as one 16-byte chunk, chunk j = c & 7 stored at position (j + g) & 7. The 8 lanes of a
+// superblock then write (8 x 16 B per lane) and read (one 16 B load per row) distinct bank
+// quads. sq: the superblock's 256 floats, 16-byte aligned.
+__device__ __forceinline__ void sb_put_sq32(float* sq, int g, const float* x) {
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+        *reinterpret_cast<float4*>(sq + 32 * g + 4 * ((j + g) & 7)) =
+            make_float4(x[j] * x[j], x[j + 8] * x[j + 8], x[j + 16] * x[j + 16], x[j + 24] * x[j + 24]);
+}
+__device__ __forceinline__ float sb_sum256_partial32(const float* sq, int lane8) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float4 v = *reinterpret_cast<const float4*>(sq + 32 * i + 4 * ((lane8 + i) & 7));
+        a0 = __fadd_rn(a0, v.x);
+        a1 = __fadd_rn(a1, v.y);
+        a2 = __fadd_rn(a2, v.z);
+        a3 = __fadd_rn(a3, v.w);
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+}
 __device__ __forceinline__ float sb_sum256_finish(const float* part8) {
     float s = 0.0f;
 #pragma unroll

@@ -46,10 +46,16 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
         float x[GS], w[GS], L[GS];
         load_row<GS>(a.src, b * QK_K + g * GS, a.src_type, x);
         if (IMAT) {
+            if constexpr (GS == 32) {
+                sb_put_sq32(sq, g, x);
+                __syncwarp();
+                s_part[sbl][g] = sb_sum256_partial32(sq, g);
+            } else {
 #pragma unroll
-            for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
-            __syncwarp();
-            if (g < 8) s_part[sbl][g] = sb_sum256_partial(sq, g);
+                for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
+                __syncwarp();
+                if (g < 8) s_part[sbl][g] = sb_sum256_partial(sq, g);
+            }
             __syncwarp();
             const float sigma2 = __fdiv_rn(Tr::SIGFAC * sb_sum256_finish(s_part[sbl]), 256.0f);
             float q[GS];
@@ -123,11 +129,18 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
             dg = f16_val(d16) * (float)(ls & 63);
             mg = f16_val(m16) * (float)(lm & 63);
         }
+        // the group's level bytes as 16-byte stores (GS / 16 per lane)
+        uint32_t pk[GS / 4];
+#pragma unroll
+        for (int i = 0; i < GS / 4; i++) pk[i] = 0u;
 #pragma unroll
         for (int i = 0; i < GS; i++) {
             const float q = dg != 0.0f ? clampf(rintf(__fdiv_rn(x[i] + mg, dg)), 0.0f, (float)Tr::NMAX) : L[i];
-            lev[g * GS + i] = (uint8_t)(int)q;
+            pk[i >> 2] |= ((uint32_t)(int)q & 0xFFu) << (8 * (i & 3));
         }
+#pragma unroll
+        for (int h = 0; h < GS / 16; h++)
+            *reinterpret_cast<uint4*>(lev + g * GS + 16 * h) = make_uint4(pk[4 * h], pk[4 * h + 1], pk[4 * h + 2], pk[4 * h + 3]);
         __syncwarp();
 
         uint8_t* o = s_out + sbl * BB;
@@ -444,10 +457,9 @@ __global__ void __launch_bounds__(IQ4XS_THREADS, IQ4XS_MIN_CTAS) iq4xs_kernel(Qu
         float x[GS], w[GS], t[GS];
         load_row<GS>(a.src, b * QK_K + g * GS, a.src_type, x);
         if (IMAT) {
-#pragma unroll
-            for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
+            sb_put_sq32(sq, g, x);
             __syncwarp();
-            if (g < 8) s_part[sbl][g] = sb_sum256_partial(sq, g);
+            s_part[sbl][g] = sb_sum256_partial32(sq, g);
             __syncwarp();
             const float sigma2 = __fdiv_rn(2.0f * sb_sum256_finish(s_part[sbl]), 256.0f);
             float q[GS];

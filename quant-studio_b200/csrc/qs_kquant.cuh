@@ -365,15 +365,31 @@ __device__ __forceinline__ float qx_search(const float* x, const float* w, float
 #pragma unroll 1
     for (int s = 0; s < 18; s++) {
         const float isc = r * (-steps[s]);
+        // adjacent pairs on f32x2, the sums still left to right. clamp(rint(.)) is the rounding add
+        // pair and a NaN-propagating clamp (as in qkx_search), and every product is f2_mul_z: a
+        // zero level or product may come out +0 where the reference's is -0. That changes only
+        // an all-zero sum's sign. sl2 <= 0 is rejected whatever its sign, and the accepted levels
+        // are rebuilt from the winning iscale below. slx == 0 can be accepted only when best < 0
+        // (negative weights); that branch sums slx again as the reference does.
         float slx = 0.0f, sl2 = 0.0f;
+        const f32x2 isc2 = f2_splat(isc), magic = f2_splat(12582912.0f), nmagic = f2_splat(-12582912.0f);
 #pragma unroll
-        for (int i = 0; i < N; i++) {
-            const float la = clampf(rint_add(isc * x[i]), -fmax, fmax - 1.0f);
-            const float a = wx[i] * la, b = (w[i] * la) * la;
-            slx = i == 0 ? a : slx + a;
-            sl2 = i == 0 ? b : sl2 + b;
+        for (int k = 0; k < N / 2; k++) {
+            float l0, l1;
+            f2_unpack(f2_add(f2_add(f2_mul_z(isc2, f2_pack(x[2 * k], x[2 * k + 1])), magic), nmagic), l0, l1);
+            const f32x2 la = f2_pack(clamp_nan(l0, -fmax, fmax - 1.0f), clamp_nan(l1, -fmax, fmax - 1.0f));
+            float a0, a1, b0, b1;
+            f2_unpack(f2_mul_z(f2_pack(wx[2 * k], wx[2 * k + 1]), la), a0, a1);
+            f2_unpack(f2_mul_z(f2_mul_z(f2_pack(w[2 * k], w[2 * k + 1]), la), la), b0, b1);
+            slx = k == 0 ? __fadd_rn(a0, a1) : __fadd_rn(__fadd_rn(slx, a0), a1);
+            sl2 = k == 0 ? __fadd_rn(b0, b1) : __fadd_rn(__fadd_rn(sl2, b0), b1);
         }
         if (sl2 > 0.0f && slx * slx > best * sl2) {
+            if (slx == 0.0f) {
+#pragma unroll
+                for (int i = 0; i < N; i++) t[i] = wx[i] * clampf(rintf(isc * x[i]), -fmax, fmax - 1.0f);
+                slx = seq_sum<N>(t);
+            }
             const float cand = __fdiv_rn(slx, sl2);
             scale = cand;
             best = cand * slx;
