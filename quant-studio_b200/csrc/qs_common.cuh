@@ -202,6 +202,29 @@ __device__ __forceinline__ float sb_sum256_partial32(const float* sq, int lane8)
     }
     return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
 }
+// 16-value groups (16 per superblock, elements 16 g + c): partial `lane8` reads columns
+// lane8 and lane8 + 8 of every row, so row g keeps the pair (c, c + 8) together as one
+// 8-byte slot, pair p = c & 7 stored at position (p + g / 2) & 7. A superblock's 16 lanes
+// write, and its 8 partial lanes read, distinct bank pairs.
+__device__ __forceinline__ void sb_put_sq16(float* sq, int g, const float* x) {
+#pragma unroll
+    for (int p = 0; p < 8; p++)
+        *reinterpret_cast<float2*>(sq + 16 * g + 2 * ((p + (g >> 1)) & 7)) = make_float2(x[p] * x[p], x[p + 8] * x[p + 8]);
+}
+__device__ __forceinline__ float sb_sum256_partial16(const float* sq, int lane8) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int pos = 2 * ((lane8 + i) & 7);  // rows 2i and 2i + 1 both rotate by i
+        const float2 v = *reinterpret_cast<const float2*>(sq + 32 * i + pos);
+        const float2 u = *reinterpret_cast<const float2*>(sq + 32 * i + 16 + pos);
+        a0 = __fadd_rn(a0, v.x);
+        a1 = __fadd_rn(a1, v.y);
+        a2 = __fadd_rn(a2, u.x);
+        a3 = __fadd_rn(a3, u.y);
+    }
+    return __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+}
 __device__ __forceinline__ float sb_sum256_finish(const float* part8) {
     float s = 0.0f;
 #pragma unroll

@@ -900,10 +900,15 @@ __global__ void __maxnreg__(IqT<TYPE>::MAXREG) iq_kernel(QuantArgs a, IqGridDev 
         // weights (iq2.py:429-431, iq2_xs.py:27-29, iq2_s.py:28-30, iq3_xxs.py:40-45)
         if (IMAT) {
             float* sq = &W.xv[0][0] + sbl * QK_K;  // xv is written only after the weights
-#pragma unroll
-            for (int i = 0; i < GS; i++) sq[gl * GS + i] = x[i] * x[i];
-            __syncwarp();
-            if (gl < 8) W.part[sbl][gl] = sb_sum256_partial(sq, gl);
+            if constexpr (GS == 32) {
+                sb_put_sq32(sq, gl, x);
+                __syncwarp();
+                W.part[sbl][gl] = sb_sum256_partial32(sq, gl);
+            } else {
+                sb_put_sq16(sq, gl, x);
+                __syncwarp();
+                if (gl < 8) W.part[sbl][gl] = sb_sum256_partial16(sq, gl);
+            }
             __syncwarp();
             const float sigma2 = __fdiv_rn(Tr::SIGFAC * sb_sum256_finish(W.part[sbl]), 256.0f);
             float qv[GS];

@@ -51,10 +51,9 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
                 __syncwarp();
                 s_part[sbl][g] = sb_sum256_partial32(sq, g);
             } else {
-#pragma unroll
-                for (int i = 0; i < GS; i++) sq[g * GS + i] = x[i] * x[i];
+                sb_put_sq16(sq, g, x);
                 __syncwarp();
-                if (g < 8) s_part[sbl][g] = sb_sum256_partial(sq, g);
+                if (g < 8) s_part[sbl][g] = sb_sum256_partial16(sq, g);
             }
             __syncwarp();
             const float sigma2 = __fdiv_rn(Tr::SIGFAC * sb_sum256_finish(s_part[sbl]), 256.0f);
@@ -146,11 +145,10 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
         uint8_t* o = s_out + sbl * BB;
         if (T == QS_Q2_K) {
             o[g] = (uint8_t)scb;
-#pragma unroll
-            for (int i = 4 * g; i < 4 * g + 4; i++) {
-                const int h = i >> 5, l = i & 31;
-                const uint8_t* q = lev + 128 * h + l;
-                o[16 + i] = (uint8_t)(q[0] | (q[32] << 2) | (q[64] << 4) | (q[96] << 6));
+            {  // bytes 4g..4g+3: levels l, l + 32, l + 64, l + 96 of half h as 2-bit fields, a word at a time
+                const int h = g >> 3, l = (4 * g) & 31;
+                const uint32_t* q = reinterpret_cast<const uint32_t*>(lev + 128 * h + l);
+                *reinterpret_cast<uint32_t*>(o + 16 + 4 * g) = q[0] | (q[8] << 2) | (q[16] << 4) | (q[24] << 6);
             }
             if (g == 0) {
                 o[80] = (uint8_t)d16; o[81] = (uint8_t)(d16 >> 8);
@@ -171,19 +169,19 @@ __global__ void __launch_bounds__(QkxTraits<T>::THREADS, QkxTraits<T>::MIN_CTAS)
             int qs0 = 16;
             if (T == QS_Q5_K) {
                 qs0 = 48;
+                // qh bytes 4g..4g+3: bit s of byte l is bit 4 of level 32 s + l, a word at a time
+                uint32_t v = 0u;
 #pragma unroll
-                for (int l = 4 * g; l < 4 * g + 4; l++) {
-                    int v = 0;
-#pragma unroll
-                    for (int s = 0; s < 8; s++) v += (lev[32 * s + l] >> 4) << s;
-                    o[16 + l] = (uint8_t)v;
-                }
+                for (int s = 0; s < 8; s++) v |= ((*reinterpret_cast<const uint32_t*>(lev + 32 * s + 4 * g) >> 4) & 0x01010101u) << s;
+                *reinterpret_cast<uint32_t*>(o + 16 + 4 * g) = v;
             }
-            const int j = g >> 1, l0 = 16 * (g & 1);
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                const uint8_t* q = lev + 64 * j + l0 + i;
-                o[qs0 + 16 * g + i] = (uint8_t)((q[0] & 0xF) | ((q[32] & 0xF) << 4));
+            {  // qs bytes 16g..16g+15: low nibbles of levels 64 j + l0 + i and 64 j + 32 + l0 + i
+                const int j = g >> 1, l0 = 16 * (g & 1);
+                const uint4 a4 = *reinterpret_cast<const uint4*>(lev + 64 * j + l0);
+                const uint4 b4 = *reinterpret_cast<const uint4*>(lev + 64 * j + 32 + l0);
+                auto nib = [](uint32_t a, uint32_t b) { return (a & 0x0F0F0F0Fu) | ((b & 0x0F0F0F0Fu) << 4); };
+                *reinterpret_cast<uint4*>(o + qs0 + 16 * g) =
+                    make_uint4(nib(a4.x, b4.x), nib(a4.y, b4.y), nib(a4.z, b4.z), nib(a4.w, b4.w));
             }
         }
         __syncthreads();
