@@ -35,6 +35,34 @@ __device__ __forceinline__ uint32_t u32_at(const uint8_t* p) {
 __device__ __forceinline__ uint32_t ksign(uint32_t i) { return i | ((__popc(i) & 1u) << 7); }
 __device__ __forceinline__ float sgn(uint32_t bits, int j) { return (bits >> j) & 1u ? -1.0f : 1.0f; }
 
+// Eight consecutive bytes as two little-endian words: one 8-byte load when aligned. Otherwise
+// the decode, which reads its staged tile in shared memory, loads the (two or three) aligned
+// words that hold them and joins them by funnel shifts (never past the word holding p[7]); the
+// error passes, which read blocks straight from global memory (BY), load the eight bytes (for
+// the unaligned 210-byte Q6_K blocks that measured faster than the word loads).
+template <bool BY>
+__device__ __forceinline__ uint2 ld8(const uint8_t* p) {
+    const uintptr_t a = (uintptr_t)p;
+    if ((a & 7) == 0) return *reinterpret_cast<const uint2*>(p);
+    if (BY) {
+        uint32_t w[2];
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+            w[k] = __byte_perm(__byte_perm(p[4 * k], p[4 * k + 1], 0x0040u), __byte_perm(p[4 * k + 2], p[4 * k + 3], 0x0040u), 0x5410u);
+        return make_uint2(w[0], w[1]);
+    }
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+    if ((a & 3) == 0) return make_uint2(w[0], w[1]);
+    const uint32_t sh = (uint32_t)(a & 3) * 8, w0 = w[0], w1 = w[1], w2 = w[2];
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+// byte i of w as a float minus `bias` (an integer): 2^23 + byte, then one exact subtraction of
+// 2^23 + bias, where (float)(byte - bias) needs an integer conversion
+template <int BIAS>
+__device__ __forceinline__ float byte_f(uint32_t w, int i) {
+    return __fadd_rn(__int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)i)), -(8388608.0f + (float)BIAS));
+}
+
 // Level -> grid value maps of the IQ dequant grids (gguf IQ*.grid_map).
 __device__ __forceinline__ float iq2_val(int l) { return l == 0 ? 8.0f : (l == 1 ? 25.0f : 43.0f); }
 __device__ __forceinline__ float iq3xxs_val(int l) { return l == 7 ? 62.0f : (float)(4 + 8 * l); }
@@ -47,13 +75,16 @@ template <int T> struct Dq;
 // Q4_0 (gguf Q4_0.dequantize_blocks): d * (q - 8); bytes hold values j (low) and j + 16 (high)
 template <> struct Dq<QS_Q4_0> {
     static constexpr int QK = 32, BB = 18;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b);
         const int p = 8 * t;
+        const uint2 q8 = ld8<BY>(b + 2 + (p & 15));
+        const uint32_t sh = p < 16 ? 0 : 4, lo = (q8.x >> sh) & 0x0F0F0F0Fu, hi = (q8.y >> sh) & 0x0F0F0F0Fu;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int q = p < 16 ? (b[2 + p + i] & 0xF) : (b[2 + p - 16 + i] >> 4);
-            v[i] = d * (float)(q - 8);
+        for (int i = 0; i < 4; i++) {
+            v[i] = d * byte_f<8>(lo, i);
+            v[4 + i] = d * byte_f<8>(hi, i);
         }
     }
 };
@@ -61,13 +92,16 @@ template <> struct Dq<QS_Q4_0> {
 // Q4_1 (gguf Q4_1.dequantize_blocks): (d * q) + m, q as in Q4_0 without the offset
 template <> struct Dq<QS_Q4_1> {
     static constexpr int QK = 32, BB = 20;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b), m = f16_at(b + 2);
         const int p = 8 * t;
+        const uint2 q8 = ld8<BY>(b + 4 + (p & 15));
+        const uint32_t sh = p < 16 ? 0 : 4, lo = (q8.x >> sh) & 0x0F0F0F0Fu, hi = (q8.y >> sh) & 0x0F0F0F0Fu;
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int q = p < 16 ? (b[4 + p + i] & 0xF) : (b[4 + p - 16 + i] >> 4);
-            v[i] = d * (float)q + m;
+        for (int i = 0; i < 4; i++) {
+            v[i] = d * byte_f<0>(lo, i) + m;
+            v[4 + i] = d * byte_f<0>(hi, i) + m;
         }
     }
 };
@@ -75,6 +109,7 @@ template <> struct Dq<QS_Q4_1> {
 // Q5_0 (gguf Q5_0.dequantize_blocks): d * ((ql | qh << 4) - 16), bit j of qh for value j
 template <> struct Dq<QS_Q5_0> {
     static constexpr int QK = 32, BB = 22;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b);
         const int p = 8 * t;
@@ -89,6 +124,7 @@ template <> struct Dq<QS_Q5_0> {
 // Q5_1 (gguf Q5_1.dequantize_blocks): (d * (ql | qh << 4)) + m
 template <> struct Dq<QS_Q5_1> {
     static constexpr int QK = 32, BB = 24;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b), m = f16_at(b + 2);
         const int p = 8 * t;
@@ -103,29 +139,42 @@ template <> struct Dq<QS_Q5_1> {
 // Q8_0 (gguf Q8_0.dequantize_blocks): x * d with x the int8 values
 template <> struct Dq<QS_Q8_0> {
     static constexpr int QK = 32, BB = 34;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b);
+        const uint2 q8 = ld8<BY>(b + 2 + 8 * t);
+        const uint32_t lo = q8.x ^ 0x80808080u, hi = q8.y ^ 0x80808080u;  // int8 + 128
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = (float)(int8_t)b[2 + 8 * t + i] * d;
+        for (int i = 0; i < 4; i++) {
+            v[i] = byte_f<128>(lo, i) * d;
+            v[4 + i] = byte_f<128>(hi, i) * d;
+        }
     }
 };
 
 // Q2_K: scales[16] qs[64] d dmin; value e: (d * (sc & 15)) * q - dmin * (sc >> 4)
 template <> struct Dq<QS_Q2_K> {
     static constexpr int QK = 256, BB = 84;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b + 80), dmin = f16_at(b + 82);
         const int e0 = 8 * t, sc = b[e0 / 16];
         const float dl = d * (float)(sc & 0xF), ml = dmin * (float)(sc >> 4);
         const int h = e0 / 128, s = (e0 % 128) / 32, l0 = e0 % 32;
+        const uint2 q8 = ld8<BY>(b + 16 + 32 * h + l0);
+        const uint32_t lo = (q8.x >> (2 * s)) & 0x03030303u, hi = (q8.y >> (2 * s)) & 0x03030303u;
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = dl * (float)((b[16 + 32 * h + l0 + i] >> (2 * s)) & 3) - ml;
+        for (int i = 0; i < 4; i++) {
+            v[i] = dl * byte_f<0>(lo, i) - ml;
+            v[4 + i] = dl * byte_f<0>(hi, i) - ml;
+        }
     }
 };
 
 // Q3_K: hmask[32] qs[64] scales[12] d; value e: (d * (sc - 32)) * (ql - 4 * !hbit)
 template <> struct Dq<QS_Q3_K> {
     static constexpr int QK = 256, BB = 110;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b + 108);
         const int e0 = 8 * t, g = e0 / 16;
@@ -133,11 +182,14 @@ template <> struct Dq<QS_Q3_K> {
         const int ls = (sc[g % 8] >> (4 * (g / 8))) & 0xF, hs = (sc[8 + g % 4] >> (2 * (g / 4))) & 3;
         const float dl = d * (float)((int)(int8_t)(uint8_t)(ls | (hs << 4)) - 32);
         const int h = e0 / 128, s = (e0 % 128) / 32, s8 = e0 / 32, l0 = e0 % 32;
+        // ql - 4 * !hbit = (ql | hbit << 2) - 4
+        const uint2 l8 = ld8<BY>(b + 32 + 32 * h + l0), h8 = ld8<BY>(b + l0);
+        const uint32_t lo = ((l8.x >> (2 * s)) & 0x03030303u) | (((h8.x >> s8) & 0x01010101u) << 2);
+        const uint32_t hi = ((l8.y >> (2 * s)) & 0x03030303u) | (((h8.y >> s8) & 0x01010101u) << 2);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int ql = (b[32 + 32 * h + l0 + i] >> (2 * s)) & 3;
-            const int qh = ((b[l0 + i] >> s8) & 1) ^ 1;
-            v[i] = dl * (float)(ql - (qh << 2));
+        for (int i = 0; i < 4; i++) {
+            v[i] = dl * byte_f<4>(lo, i);
+            v[4 + i] = dl * byte_f<4>(hi, i);
         }
     }
 };
@@ -156,30 +208,40 @@ __device__ __forceinline__ void k_scale_min(const uint8_t* s, int j, int& sc, in
 // Q4_K: d dmin scales[12] qs[128]; value e: (d * sc) * q - dmin * m
 template <> struct Dq<QS_Q4_K> {
     static constexpr int QK = 256, BB = 144;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b), dmin = f16_at(b + 2);
         const int e0 = 8 * t, sub = e0 / 32, c = e0 / 64, s = (e0 % 64) / 32, l0 = e0 % 32;
         int sc, mn;
         k_scale_min(b + 4, sub, sc, mn);
         const float dl = d * (float)sc, ml = dmin * (float)mn;
+        const uint2 q8 = ld8<BY>(b + 16 + 32 * c + l0);
+        const uint32_t lo = (q8.x >> (4 * s)) & 0x0F0F0F0Fu, hi = (q8.y >> (4 * s)) & 0x0F0F0F0Fu;
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = dl * (float)((b[16 + 32 * c + l0 + i] >> (4 * s)) & 0xF) - ml;
+        for (int i = 0; i < 4; i++) {
+            v[i] = dl * byte_f<0>(lo, i) - ml;
+            v[4 + i] = dl * byte_f<0>(hi, i) - ml;
+        }
     }
 };
 
 // Q5_K: d dmin scales[12] qh[32] qs[128]
 template <> struct Dq<QS_Q5_K> {
     static constexpr int QK = 256, BB = 176;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b), dmin = f16_at(b + 2);
         const int e0 = 8 * t, sub = e0 / 32, c = e0 / 64, s = (e0 % 64) / 32, l0 = e0 % 32;
         int sc, mn;
         k_scale_min(b + 4, sub, sc, mn);
         const float dl = d * (float)sc, ml = dmin * (float)mn;
+        const uint2 l8 = ld8<BY>(b + 48 + 32 * c + l0), h8 = ld8<BY>(b + 16 + l0);
+        const uint32_t lo = ((l8.x >> (4 * s)) & 0x0F0F0F0Fu) | (((h8.x >> sub) & 0x01010101u) << 4);
+        const uint32_t hi = ((l8.y >> (4 * s)) & 0x0F0F0F0Fu) | (((h8.y >> sub) & 0x01010101u) << 4);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int q = ((b[48 + 32 * c + l0 + i] >> (4 * s)) & 0xF) | (((b[16 + l0 + i] >> sub) & 1) << 4);
-            v[i] = dl * (float)q - ml;
+        for (int i = 0; i < 4; i++) {
+            v[i] = dl * byte_f<0>(lo, i) - ml;
+            v[4 + i] = dl * byte_f<0>(hi, i) - ml;
         }
     }
 };
@@ -187,16 +249,19 @@ template <> struct Dq<QS_Q5_K> {
 // Q6_K: ql[128] qh[64] scales[16] (int8) d; value e: (d * sc) * (q - 32)
 template <> struct Dq<QS_Q6_K> {
     static constexpr int QK = 256, BB = 210;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b + 208);
         const int e0 = 8 * t;
         const float dl = d * (float)(int8_t)b[192 + e0 / 16];
         const int c = e0 / 128, sl = (e0 % 128) / 64, ll = e0 % 64, sh = (e0 % 128) / 32, lh = e0 % 32;
+        const uint2 l8 = ld8<BY>(b + 64 * c + ll), h8 = ld8<BY>(b + 128 + 32 * c + lh);
+        const uint32_t lo = ((l8.x >> (4 * sl)) & 0x0F0F0F0Fu) | (((h8.x >> (2 * sh)) & 0x03030303u) << 4);
+        const uint32_t hi = ((l8.y >> (4 * sl)) & 0x0F0F0F0Fu) | (((h8.y >> (2 * sh)) & 0x03030303u) << 4);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int ql = (b[64 * c + ll + i] >> (4 * sl)) & 0xF;
-            const int qh = (b[128 + 32 * c + lh + i] >> (2 * sh)) & 3;
-            v[i] = dl * (float)((int)(int8_t)(uint8_t)(ql | (qh << 4)) - 32);
+        for (int i = 0; i < 4; i++) {
+            v[i] = dl * byte_f<32>(lo, i);
+            v[4 + i] = dl * byte_f<32>(hi, i);
         }
     }
 };
@@ -204,6 +269,7 @@ template <> struct Dq<QS_Q6_K> {
 // IQ2_XXS: d, 8 x (4 grid bytes, u32 of 4 x 7 sign bits | scale << 28)
 template <> struct Dq<QS_IQ2_XXS> {
     static constexpr int QK = 256, BB = 66;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
         const float d = f16_at(b);
         const int g = t / 4, s = t % 4;
@@ -219,6 +285,7 @@ template <> struct Dq<QS_IQ2_XXS> {
 // IQ2_XS: d, 32 x u16 (9-bit grid index | 7-bit sign index << 9), 8 bytes of 4-bit scales
 template <> struct Dq<QS_IQ2_XS> {
     static constexpr int QK = 256, BB = 74;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
         const float d = f16_at(b);
         const int q16 = b[2 + 2 * t] | (b[3 + 2 * t] << 8);
@@ -234,6 +301,7 @@ template <> struct Dq<QS_IQ2_XS> {
 // IQ2_S: d, qs[32], signs[32], qh[8] (2 high index bits each), scales[8]
 template <> struct Dq<QS_IQ2_S> {
     static constexpr int QK = 256, BB = 82;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
         const float d = f16_at(b);
         const int sc = (b[74 + t / 4] >> (4 * ((t / 2) & 1))) & 0xF;
@@ -249,6 +317,7 @@ template <> struct Dq<QS_IQ2_S> {
 // IQ3_XXS: d, qs[64] grid bytes (4 values each), 8 x u32 (4 x 7 sign bits | scale << 28)
 template <> struct Dq<QS_IQ3_XXS> {
     static constexpr int QK = 256, BB = 98;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
         const float d = f16_at(b);
         const int g = t / 4, s = t % 4;
@@ -267,6 +336,7 @@ template <> struct Dq<QS_IQ3_XXS> {
 // IQ3_S: d, qs[64], qh[8] (high index bit), signs[32], scales[4]; db = d * (1 + 2 * sc)
 template <> struct Dq<QS_IQ3_S> {
     static constexpr int QK = 256, BB = 110;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t* kgrid, float* v) {
         const float d = f16_at(b);
         const int g = t / 4;
@@ -288,6 +358,7 @@ template <> struct Dq<QS_IQ3_S> {
 // IQ4_XS: d, scales_h (u16), scales_l[4], qs[128]; value: (d * (sc - 32)) * kvalues[q]
 template <> struct Dq<QS_IQ4_XS> {
     static constexpr int QK = 256, BB = 136;
+    template <bool BY>
     __device__ static void decode(const uint8_t* b, int t, const uint16_t*, float* v) {
         const float d = f16_at(b);
         const int i = t / 4, u = (t % 4) / 2, j0 = 8 * (t % 2);
@@ -315,9 +386,9 @@ struct DqArgs {
 
 __device__ __forceinline__ void load_x8(const void* base, int64_t e0, int src, float* v) { load_row<8>(base, e0, src, v); }
 
-// resident CTAs per SM the register budget is sized for: the decode keeps little live
-// across the staging; the checkers hold the prefetched source values and weights
-template <int MODE> struct DqOcc { static constexpr int CTAS = MODE == DQ_DECODE ? 5 : 4; };
+// resident CTAs per SM the register budget is sized for (64 registers): the checkers hold the
+// prefetched source values and weights; the decode's word loads spilled at five
+template <int MODE> struct DqOcc { static constexpr int CTAS = 4; };
 
 template <int TYPE, int MODE>
 __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArgs a) {
@@ -396,7 +467,7 @@ __global__ void __launch_bounds__(DQ_THREADS, DqOcc<MODE>::CTAS) dq_kernel(DqArg
         }
         if (live) {
             float v[8];
-            D::decode(tb + lb * D::BB, t, a.kgrid, v);
+            D::template decode<MODE != DQ_DECODE>(tb + lb * D::BB, t, a.kgrid, v);
             if (MODE == DQ_DECODE) {
                 const int64_t row = b / a.nblk_row, col = (b - row * a.nblk_row) * D::QK + 8 * t;
                 float4* o = reinterpret_cast<float4*>(a.dst + row * a.dst_stride + col);
