@@ -855,6 +855,24 @@ __device__ __forceinline__ void iq_decode(const uint16_t* win, const uint16_t* k
 
 template <class Tr>
 __device__ __forceinline__ void iq_sums(const float* w, const float* wx, const float* q, float& sumqx, float& sumq2) {
+    if constexpr (Tr::SUMK == SUM_TREE) {
+        // on f32x2 pairs (v[k], v[k + H]), tree_sum2 keeping the adjacent-pair order. The grid
+        // values are positive, so a product is zero only for a zero weight or value, and
+        // f2_mul_z's +0 for -0 changes only an all-zero sum's sign: sumq2 <= 0 is rejected
+        // either way, and sumqx == 0 is never accepted (best >= 0) and refits to a zero scale,
+        // which neither flips the signs nor changes the 4-bit sub-scale
+        constexpr int H = Tr::GS / 2;
+        f32x2 a2[H], b2[H];
+#pragma unroll
+        for (int k = 0; k < H; k++) {
+            const f32x2 q2 = f2_pack(q[k], q[k + H]);
+            a2[k] = f2_mul_z(f2_pack(wx[k], wx[k + H]), q2);
+            b2[k] = f2_mul_z(f2_mul_z(f2_pack(w[k], w[k + H]), q2), q2);
+        }
+        sumqx = tree_sum2<H>(a2);
+        sumq2 = tree_sum2<H>(b2);
+        return;
+    }
     float a[Tr::GS], b[Tr::GS];
 #pragma unroll
     for (int i = 0; i < Tr::GS; i++) {
