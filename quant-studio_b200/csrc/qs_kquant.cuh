@@ -369,8 +369,11 @@ __device__ __forceinline__ float qx_search(const float* x, const float* w, float
         // pair and a NaN-propagating clamp (as in qkx_search), and every product is f2_mul_z: a
         // zero level or product may come out +0 where the reference's is -0. That changes only
         // an all-zero sum's sign. sl2 <= 0 is rejected whatever its sign, and the accepted levels
-        // are rebuilt from the winning iscale below. slx == 0 can be accepted only when best < 0
-        // (negative weights); that branch sums slx again as the reference does.
+        // are rebuilt from the winning iscale below. slx == 0 passes the accept test only when
+        // best < 0 (negative weights), and there the reference's zero is +0 as well: with isc > 0
+        // the positively weighted nonzero level that sl2 > 0 needs gives a +0 or positive term,
+        // with isc < 0 the negatively weighted one that made best < 0 does. The branch that sums
+        // slx again as the reference does is a guard that gives the same value.
         float slx = 0.0f, sl2 = 0.0f;
         const f32x2 isc2 = f2_splat(isc), magic = f2_splat(12582912.0f), nmagic = f2_splat(-12582912.0f);
 #pragma unroll
