@@ -162,28 +162,15 @@ __device__ __forceinline__ float min_of(const float* x) {
     return m;
 }
 
-// torch's `(x*x).sum(-1)` over a 256-element superblock, from squares laid out in
-// shared memory: 32 vectors of 8 lanes, four accumulators over vectors 4i+k, then a
-// left-to-right pass over the 8 lane partials. `lane8` in [0, 8) computes partial
-// `lane8`; the caller reduces the 8 partials with sb_sum256_finish.
-__device__ __forceinline__ float sb_sum256_partial(const float* sq, int lane8) {
-    float acc[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        float a = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; i++) a = __fadd_rn(a, sq[8 * (4 * i + k) + lane8]);
-        acc[k] = a;
-    }
-    return __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
-}
-
-// The same sum for 32-value groups (8 per superblock, group g's values x[0..31] are elements
-// 32 g + c), from a layout without bank conflicts. Partial `lane8` reads the columns
-// c = lane8 + 8 k (k = 0..3) of every group row, so row g keeps those four columns together
-// as one 16-byte chunk, chunk j = c & 7 stored at position (j + g) & 7. The 8 lanes of a
-// superblock then write (8 x 16 B per lane) and read (one 16 B load per row) distinct bank
-// quads. sq: the superblock's 256 floats, 16-byte aligned.
+// torch's `(x*x).sum(-1)` over a 256-element superblock: 32 vectors of 8 lanes, four
+// accumulators over vectors 4i+k, then a left-to-right pass over the 8 lane partials. Partial
+// `lane8` in [0, 8) sums elements 32 i + 8 k + lane8 over i for each k; the caller reduces the
+// 8 partials with sb_sum256_finish. The squares go through shared memory in a layout without
+// bank conflicts. For 32-value groups (8 per superblock, group g's values are elements
+// 32 g + c), partial `lane8` reads the columns c = lane8 + 8 k (k = 0..3) of every group row, so
+// row g keeps those four columns together as one 16-byte chunk, chunk j = c & 7 stored at
+// position (j + g) & 7. The 8 lanes of a superblock then write (8 x 16 B per lane) and read
+// (one 16 B load per row) distinct bank quads. sq: the superblock's 256 floats, 16-byte aligned.
 __device__ __forceinline__ void sb_put_sq32(float* sq, int g, const float* x) {
 #pragma unroll
     for (int j = 0; j < 8; j++)

@@ -871,20 +871,15 @@ __device__ __forceinline__ void iq_sums(const float* w, const float* wx, const f
         }
         sumqx = tree_sum2<H>(a2);
         sumq2 = tree_sum2<H>(b2);
-        return;
-    }
-    float a[Tr::GS], b[Tr::GS];
+    } else {  // torch's `.sum(-1)` order (IQ2_XXS), scalar
+        float a[Tr::GS], b[Tr::GS];
 #pragma unroll
-    for (int i = 0; i < Tr::GS; i++) {
-        a[i] = wx[i] * q[i];  // (w x) q
-        b[i] = (w[i] * q[i]) * q[i];
-    }
-    if (Tr::SUMK == SUM_TORCH) {
+        for (int i = 0; i < Tr::GS; i++) {
+            a[i] = wx[i] * q[i];  // (w x) q
+            b[i] = (w[i] * q[i]) * q[i];
+        }
         sumqx = torch_sum<Tr::GS>(a);
         sumq2 = torch_sum<Tr::GS>(b);
-    } else {
-        sumqx = tree_sum<Tr::GS>(a);
-        sumq2 = tree_sum<Tr::GS>(b);
     }
 }
 

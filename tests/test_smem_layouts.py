@@ -5,7 +5,7 @@ numpy so that a layout change that reorders a sum, or a bank-conflict regression
 
 * the superblock squares of csrc/qs_common.cuh (sb_put_sq32 / sb_sum256_partial32 for
   32-value groups, sb_put_sq16 / sb_sum256_partial16 for 16-value groups) read back, in
-  torch's `.sum(-1)` order, exactly the elements the row-major sb_sum256_partial reads, and
+  torch's `.sum(-1)` order, exactly the elements of a row-major layout, and
   their writer and reader phases touch distinct banks;
 * the word-wide level packing of csrc/qs_kquant.cu (Q2_K crumbs, Q4_K / Q5_K nibbles, Q5_K
   high bits) equals the byte-by-byte packing;
@@ -20,7 +20,7 @@ RNG = np.random.default_rng(11)
 
 # --- superblock squares ------------------------------------------------------------------
 def partial_rowmajor(sq: np.ndarray, lane8: int) -> np.float32:
-    """sb_sum256_partial: acc_k = sum over i of sq[32 i + 8 k + lane8], then ((a0+a1)+a2)+a3."""
+    """torch's order on row-major squares: acc_k = sum over i of sq[32 i + 8 k + lane8], then ((a0+a1)+a2)+a3."""
     acc = []
     for k in range(4):
         a = np.float32(0.0)
